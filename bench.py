@@ -1,0 +1,282 @@
+"""Benchmark of batched use_model: inference samples/s on 1..8 B200s.
+
+One step = one batched use_model over the workload's batch of synthetic samples
+on every GPU (weak scaling: each rank runs the full per-GPU batch on its own
+GPU; samples are sharded, weights replicated, no collective on the data path).
+
+  value     samples/s of the whole job, inputs resident in HBM, timed with CUDA
+            events on the launching stream (max over ranks)
+  e2e       the same through the host-array C-ABI call (rosenna_use_model_f32):
+            H2D of the step's inputs from pinned memory, kernels, D2H of outputs
+  roofline  the dominant kernel's achieved FLOP/s against the measured FP32 peak
+            (cuBLAS SGEMM with TF32 off, timed here), plus DRAM traffic per launch
+            from the committed ncu capture
+  cpu_baseline  the fp64 oracle (a C restatement of roseNNa's Fortran path,
+            use_model once per sample, all host threads) on a bounded sample
+
+Default workload: the wide MLP (16-256x5-8, ReLU), batch 4,194,304 per GPU.
+`--impl reference` times roseNNa's algorithm on the host cores instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
+# capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC = {}
+
+DEFAULT_WORKLOAD = "wide_mlp"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    p.add_argument("--batch", type=int, default=0, help="per-GPU batch (default: the workload's)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def cpu_baseline(name, model_dir, target_seconds=12.0, steps=1):
+    """fp64 oracle, use_model once per sample over all host threads."""
+    from oracle import oracle as O
+    from rosenna_b200 import workloads
+
+    m = O.OracleModel(model_dir)
+    threads = O.max_threads()
+    # calibrate on a small sample, then size the sample for ~target_seconds
+    n = max(64, threads * 8)
+    ins = workloads.make_inputs(name, n, seed_offset=99)
+    t0 = time.perf_counter()
+    m.run_batched(n, ins, [1] * len(ins), [1], threads)
+    dt = time.perf_counter() - t0
+    n = int(max(threads, min(1 << 22, n * target_seconds / max(dt, 1e-6) / steps)))
+    ins = workloads.make_inputs(name, n, seed_offset=98)
+    rates = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        m.run_batched(n, ins, [1] * len(ins), [1], threads)
+        rates.append(n / (time.perf_counter() - t0))
+    return {"value": statistics.median(rates), "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{n} samples of the workload per step, fp64, use_model per sample (C restatement of "
+                      f"fLibrary/layers.f90; no Fortran compiler in the image)"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.dev), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_fp32_peak(torch):
+    """cuBLAS SGEMM (TF32 off), 8192^3, best of 5: the FP32 FFMA denominator."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    a = torch.randn(8192, 8192, device="cuda")
+    b = torch.randn(8192, 8192, device="cuda")
+    for _ in range(2):
+        torch.mm(a, b)
+    best = 0.0
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = max(best, 2 * 8192 ** 3 / (e0.elapsed_time(e1) / 1e3))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    torch.cuda.empty_cache()
+    return best / 1e12
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    from rosenna_b200 import workloads
+
+    w = workloads.WORKLOADS[args.workload]
+    with tempfile.TemporaryDirectory() as d:
+        workloads.write_model(args.workload, d)
+        cb = cpu_baseline(args.workload, d, target_seconds=max(2.0, 60.0 / max(1, args.steps + args.warmup)),
+                          steps=max(1, args.steps))
+    line = {"metric": "inference samples/sec (batched use_model)", "value": cb["value"], "unit": "samples/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"{w.name}: {w.description}", "batch_per_gpu": w.batch,
+                       "parallelism": "host cores (use_model per sample)"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from rosenna_b200 import api, workloads
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    w = workloads.WORKLOADS[args.workload]
+    n = args.batch or w.batch
+    tmp = tempfile.TemporaryDirectory()
+    workloads.write_model(args.workload, tmp.name)
+    api.set_devices([local])
+    api.initialize(tmp.name)
+    ins = workloads.make_inputs_torch(args.workload, n, device="cuda", seed_offset=rank)
+    outs = [torch.empty((r, n), dtype=torch.float32, device="cuda") for r in w.output_rows]
+    in_ptrs, out_ptrs = [x.data_ptr() for x in ins], [o.data_ptr() for o in outs]
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident throughput ----
+    for _ in range(max(3, args.warmup)):
+        api.use_model_device(n, in_ptrs, out_ptrs, stream.cuda_stream)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            api.use_model_device(n, in_ptrs, out_ptrs, stream.cuda_stream)
+            launches += api.last_launch_count()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    barrier()
+    torch.cuda.synchronize()
+    value = world * n * args.steps / t_dev
+    plan = api.plan_description()
+    launches_per_step = launches // max(1, args.steps)
+
+    # ---- end to end through the host-array C ABI (pinned host buffers) ----
+    h_in = [x.cpu().pin_memory() for x in ins]
+    h_out = [torch.empty((r, n), dtype=torch.float32).pin_memory() for r in w.output_rows]
+    hi, ho = [x.data_ptr() for x in h_in], [o.data_ptr() for o in h_out]
+    api.use_model_ptrs(n, hi, ho)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        api.use_model_ptrs(n, hi, ho)
+    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    e2e = {"value": world * n * args.steps / t_e2e, "unit": "samples/s",
+           "h2d_bytes_per_step": sum(x.numel() * 4 for x in h_in), "d2h_bytes_per_step": sum(o.numel() * 4 for o in h_out),
+           "api": "rosenna_use_model_f32 (host arrays, pinned)"}
+    ok_out = bool(torch.isfinite(h_out[0]).all())
+
+    # ---- roofline of the dominant kernel ----
+    fp32_peak = measured_fp32_peak(torch) if rank == 0 else None
+    kernel_s = t_dev / max(1, args.steps * launches_per_step) if launches_per_step == 1 else None
+    achieved = (w.flops_per_sample * n) / kernel_s / 1e12 if kernel_s else None
+    roof = {"bound": "fp32", "kernel": "mlp_ffma_kernel" if "mlp" in args.workload else "plan",
+            "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+            "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
+            "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (MEASURED_PEAKS.json has no FP32 figure)",
+            "traffic": NCU_TRAFFIC.get(args.workload),
+            "algorithmic_flops_per_launch": w.flops_per_sample * n if kernel_s else None}
+
+    if rank == 0:
+        cb = None
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_baseline(args.workload, tmp.name)
+        line = {"metric": "inference samples/sec (batched use_model)", "value": value, "unit": "samples/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"{w.name}: {w.description}", "batch_per_gpu": n, "global_batch": world * n,
+                           "parallelism": f"dp{world} (contiguous sample shards, weights replicated, no collective)",
+                           "l2": f"inputs {sum(x.numel() * 4 for x in ins) / 1e6:.0f} MB + outputs "
+                                 f"{sum(o.numel() * 4 for o in outs) / 1e6:.0f} MB per step exceed the 126 MB L2",
+                           "plan": plan.strip().splitlines()},
+                "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cb,
+                "clocks": clk.summary(), "outputs_finite": ok_out}
+        print(json.dumps(line), flush=True)
+    api.finalize()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

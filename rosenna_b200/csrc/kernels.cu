@@ -1,0 +1,513 @@
+// sm_100a kernels of the launch plan.
+//
+// Layout (all kernels): a batched tensor is rows x n floats, row r of sample s at
+// base[r * ld + s]; consecutive threads own consecutive samples, so every global
+// access is a coalesced row segment.
+//
+// mlp_ffma  : a whole Gemm+bias+activation chain (fLibrary/layers.f90:11-23 and
+//             activation_funcs.f90) per tile of S samples.  Activations stay in
+//             shared memory between layers; weights stream through a cp.async
+//             double buffer in 32-row chunks; each thread owns an 8x8 register
+//             tile (8 outputs x 8 samples) of every layer's product.
+// lstm_ffma : persistent time loop of one LSTM layer (layers.f90:62-132) per
+//             tile of S samples: [W_ih | W_hh] resident in shared memory with
+//             each unit's four gates in adjacent columns, so one thread's tile
+//             holds all gates of two units and updates their cell state in
+//             registers; h_t goes back to shared memory for step t+1.
+// conv_pool : direct convolution (layers.f90:183-233) + ReLU + max/avg pool
+//             (layers.f90:236-310) with zero padding, one thread per sample
+//             and pooled output element.
+#include "kernels.cuh"
+
+#include <algorithm>
+
+namespace rosenna {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kKC = 32;  // weight rows per streamed chunk
+constexpr size_t kMaxSmem = 227 * 1024;
+
+// ---- activations -----------------------------------------------------------
+// tanh(x) = 1 - 2 / (1 + e^{2x}) and sigmoid(x) = 1 / (1 + e^{-x}), with
+// e^y = 2^(y log2 e) from the hardware exp2 unit and a hardware reciprocal.
+// Absolute error ~2e-7, far inside the 1e-5 tolerance against the fp64 path.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float act_tanh(float x) {
+    return 1.f - 2.f * rcp_approx(1.f + ex2_approx(2.8853900817779268f * x));
+}
+__device__ __forceinline__ float act_sigmoid(float x) { return rcp_approx(1.f + ex2_approx(-1.4426950408889634f * x)); }
+__device__ __forceinline__ float apply_act(float v, int act) {
+    switch (act) {
+        case 1: return v < 0.f ? 0.f : v;  // relu: `where (x < 0) 0 elsewhere x`
+        case 2: return act_tanh(v);
+        case 3: return act_sigmoid(v);
+        default: return v;
+    }
+}
+
+// ---- cp.async helpers ------------------------------------------------------
+__device__ __forceinline__ unsigned smem_addr(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(dst)), "l"(src));
+}
+// 4-byte copy; src_bytes == 0 writes zero without reading src
+__device__ __forceinline__ void cp_async4(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Copies rows [r0, r0+nr) x samples [0, S) of a batched tensor into shared
+// memory (row stride S), zero-filling rows >= rows_valid and samples >= nval.
+__device__ __forceinline__ void stage_rows(float *dst, const float *src, long long ld, int r0, int nr, int rows_valid,
+                                           int S, int nval, bool vec_ok) {
+    const int q4 = S >> 2;
+    for (int i = threadIdx.x; i < nr * q4; i += blockDim.x) {
+        int r = i / q4, q = (i - r * q4) << 2, row = r0 + r;
+        float *d = dst + r * S + q;
+        const float *s = src + (long long)row * ld + q;
+        if (row < rows_valid && vec_ok && q + 4 <= nval) {
+            cp_async16(d, s);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                bool ok = row < rows_valid && q + e < nval;
+                cp_async4(d + e, ok ? (const void *)(s + e) : (const void *)src, ok ? 4 : 0);
+            }
+        }
+    }
+}
+
+// ---- fused MLP ---------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ MlpLayerDev L[kMaxMlpLayers];
+    const int tid = threadIdx.x, S = p.S, nl = p.nlayers;
+    if (tid < nl) L[tid] = p.layers[tid];
+    float *act[2] = {sm, sm + (size_t)p.hid_rows * S};
+    float *stW[2], *stA[2];
+    stW[0] = act[1] + (size_t)p.hid_rows * S;
+    stW[1] = stW[0] + kKC * p.max_mp;
+    stA[0] = stW[1] + kKC * p.max_mp;
+    stA[1] = stA[0] + (size_t)p.stage_a_rows * S;
+    float *bias = stA[1] + (size_t)p.stage_a_rows * S;
+    __syncthreads();
+    {
+        int bo = 0;
+        for (int l = 0; l < nl; l++) {
+            for (int i = tid; i < L[l].Mp; i += kThreads) bias[bo + i] = p.arena[L[l].b_off + i];
+            bo += L[l].Mp;
+        }
+    }
+    const long long ntiles = (p.n + S - 1) / S;
+    long long tile = blockIdx.x;
+    if (tile >= ntiles) return;
+    const bool in_vec = ((p.ld_in & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.in) & 15) == 0);
+
+    auto issue = [&](long long t, int l, int c, int st) {
+        const int k0 = c * kKC, kc = min(kKC, L[l].Kp - k0), mp = L[l].Mp;
+        const float *src = p.arena + L[l].w_off + (long long)k0 * mp;
+        const int nv = kc * mp / 4;
+        for (int i = tid; i < nv; i += kThreads) cp_async16(stW[st] + 4 * i, src + 4 * i);
+        if (l == 0) {
+            long long n0 = t * S;
+            int nval = (int)min((long long)S, p.n - n0);
+            stage_rows(stA[st], p.in + n0, p.ld_in, k0, kc, L[0].K, S, nval, in_vec && (n0 & 3) == 0);
+        }
+        cp_async_commit();
+    };
+
+    int st = 0;
+    issue(tile, 0, 0, 0);
+    for (; tile < ntiles; tile += gridDim.x) {
+        const long long n0 = tile * S;
+        const int nval = (int)min((long long)S, p.n - n0);
+        int bo = 0;
+        for (int l = 0; l < nl; l++) {
+            const int Mp = L[l].Mp, Kp = L[l].Kp;
+            const int mg_n = Mp >> 3, sg_n = S >> 3;
+            const bool active = tid < mg_n * sg_n;
+            const int mg = tid % mg_n, sg = tid / mg_n;
+            const int m0 = mg * 4, s0 = sg * 4, mh = Mp >> 1, sh = S >> 1;
+            const float *aprev = act[(l + 1) & 1];
+            float acc[8][8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+            const int nch = (Kp + kKC - 1) / kKC;
+            for (int c = 0; c < nch; c++) {
+                cp_async_wait_all();
+                __syncthreads();
+                // prefetch the next chunk of the cyclic (tile, layer, chunk) sequence
+                if (c + 1 < nch) issue(tile, l, c + 1, st ^ 1);
+                else if (l + 1 < nl) issue(tile, l + 1, 0, st ^ 1);
+                else if (tile + gridDim.x < ntiles) issue(tile + gridDim.x, 0, 0, st ^ 1);
+                if (active) {
+                    const float *W = stW[st];
+                    const float *A = (l == 0) ? stA[st] : aprev + (size_t)c * kKC * S;
+                    const int kc = min(kKC, Kp - c * kKC);
+#pragma unroll 4
+                    for (int kk = 0; kk < kc; kk++) {
+                        const float4 a0 = *reinterpret_cast<const float4 *>(A + kk * S + s0);
+                        const float4 a1 = *reinterpret_cast<const float4 *>(A + kk * S + sh + s0);
+                        const float4 w0 = *reinterpret_cast<const float4 *>(W + kk * Mp + m0);
+                        const float4 w1 = *reinterpret_cast<const float4 *>(W + kk * Mp + mh + m0);
+                        const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+#pragma unroll
+                            for (int j = 0; j < 8; j++) acc[i][j] = fmaf(w[i], a[j], acc[i][j]);
+                    }
+                }
+                st ^= 1;
+            }
+            if (active) {
+                const int actf = L[l].act;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int m = (i < 4 ? m0 + i : mh + m0 + i - 4);
+                    const float b = bias[bo + m];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = apply_act(acc[i][j] + b, actf);
+                }
+                if (l + 1 < nl) {
+                    float *O = act[l & 1];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int m = (i < 4 ? m0 + i : mh + m0 + i - 4);
+                        *reinterpret_cast<float4 *>(O + (size_t)m * S + s0) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+                        *reinterpret_cast<float4 *>(O + (size_t)m * S + sh + s0) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+                    }
+                } else {
+                    const int M = L[l].M;
+                    const bool vec = ((p.ld_out & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) && ((n0 & 3) == 0);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int m = (i < 4 ? m0 + i : mh + m0 + i - 4);
+                        if (m >= M) continue;
+                        float *o = p.out + (long long)m * p.ld_out + n0;
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int s = (h ? sh : 0) + s0;
+                            if (vec && s + 4 <= nval) {
+                                *reinterpret_cast<float4 *>(o + s) =
+                                    make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+                            } else {
+#pragma unroll
+                                for (int e = 0; e < 4; e++)
+                                    if (s + e < nval) o[s + e] = acc[i][4 * h + e];
+                            }
+                        }
+                    }
+                }
+            }
+            bo += Mp;
+        }
+    }
+    cp_async_wait_all();
+}
+
+// ---- LSTM ----------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p) {
+    extern __shared__ __align__(16) float sm[];
+    const int tid = threadIdx.x, S = p.S, Ip = p.Ip, Hp = p.Hp, G = 4 * Hp, K = Ip + Hp;
+    float *W = sm;                        // [K][G]
+    float *bias = W + (size_t)K * G;      // [G]
+    float *act[2] = {bias + G, bias + G + (size_t)K * S};  // [K][S] each: rows 0..Ip-1 = x_t, Ip.. = h
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(p.arena + p.w_off);
+        for (int i = tid; i < K * G / 4; i += kThreads) cp_async16(W + 4 * i, src + i);
+        for (int i = tid; i < G; i += kThreads) bias[i] = p.arena[p.b_off + i];
+        cp_async_commit();
+    }
+    const int mg_n = Hp >> 1, sg_n = S >> 3;
+    const bool active = tid < mg_n * sg_n;
+    const int mg = tid % mg_n, sg = tid / mg_n;
+    const int s0 = sg * 4, sh = S >> 1;
+    const int c0l = mg * 4, c1l = G / 2 + mg * 4;  // gate columns of the two units
+    const int u0 = mg, u1 = Hp / 2 + mg;           // the two units
+    const bool x_vec = ((p.ld_x & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
+    const long long ntiles = (p.n + S - 1) / S;
+    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const long long n0 = tile * S;
+        const int nval = (int)min((long long)S, p.n - n0);
+        const bool vec = x_vec && (n0 & 3) == 0;
+        __syncthreads();  // previous tile finished with act[]
+        // x_0 into act[0] rows [0, Ip) (rows >= I zero); zero the padding rows of act[1]
+        stage_rows(act[0], p.x + n0, (long long)p.T * p.ld_x, 0, Ip, p.I, S, nval, vec);
+        for (int i = tid; i < (Ip - p.I) * S; i += kThreads) act[1][p.I * S + i] = 0.f;
+        // h0 into act[0] rows [Ip, Ip+Hp)
+        for (int i = tid; i < Hp * S; i += kThreads) {
+            int j = i / S, s = i - j * S;
+            float v = 0.f;
+            if (j < p.H && s < nval) {
+                if (p.h0) v = p.h0[(long long)j * p.ld_h0 + n0 + s];
+                else if (p.h0_const >= 0) v = p.arena[p.h0_const + j];
+            }
+            act[0][(Ip + j) * S + s] = v;
+        }
+        cp_async_commit();
+        float c[2][8], h[2][8];
+#pragma unroll
+        for (int u = 0; u < 2; u++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int unit = u ? u1 : u0, s = (j < 4 ? s0 + j : sh + s0 + j - 4);
+                float v = 0.f;
+                if (active && unit < p.H && s < nval) {
+                    if (p.c0) v = p.c0[(long long)unit * p.ld_c0 + n0 + s];
+                    else if (p.c0_const >= 0) v = p.arena[p.c0_const + unit];
+                }
+                c[u][j] = v;
+                h[u][j] = 0.f;
+            }
+        cp_async_wait_all();
+        __syncthreads();
+        for (int t = 0; t < p.T; t++) {
+            const float *A = act[t & 1];
+            float *Nx = act[(t + 1) & 1];
+            if (t + 1 < p.T) {
+                // x_{t+1}: row (t+1) + T*i of the input
+                stage_rows(Nx, p.x + (long long)(t + 1) * p.ld_x + n0, (long long)p.T * p.ld_x, 0, p.I, p.I, S, nval,
+                           vec && ((p.ld_x * (t + 1)) & 3) == 0);
+                cp_async_commit();
+            }
+            if (active) {
+                float acc[8][8];
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+#pragma unroll 4
+                for (int k = 0; k < K; k++) {
+                    const float4 a0 = *reinterpret_cast<const float4 *>(A + k * S + s0);
+                    const float4 a1 = *reinterpret_cast<const float4 *>(A + k * S + sh + s0);
+                    const float4 w0 = *reinterpret_cast<const float4 *>(W + k * G + c0l);
+                    const float4 w1 = *reinterpret_cast<const float4 *>(W + k * G + c1l);
+                    const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+#pragma unroll
+                        for (int j = 0; j < 8; j++) acc[i][j] = fmaf(w[i], a[j], acc[i][j]);
+                }
+                // gates of unit u are acc rows 4u..4u+3 (i, f, g, o), layers.f90:88-96
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const int cb = u ? c1l : c0l, unit = u ? u1 : u0;
+                    const float bi = bias[cb], bf = bias[cb + 1], bg = bias[cb + 2], bo = bias[cb + 3];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float ig = act_sigmoid(acc[4 * u][j] + bi);
+                        const float fg = act_sigmoid(acc[4 * u + 1][j] + bf);
+                        const float gg = act_tanh(acc[4 * u + 2][j] + bg);
+                        const float og = act_sigmoid(acc[4 * u + 3][j] + bo);
+                        c[u][j] = fg * c[u][j] + ig * gg;
+                        h[u][j] = og * act_tanh(c[u][j]);
+                    }
+                    float *hr = Nx + (size_t)(Ip + unit) * S;
+                    *reinterpret_cast<float4 *>(hr + s0) = make_float4(h[u][0], h[u][1], h[u][2], h[u][3]);
+                    *reinterpret_cast<float4 *>(hr + sh + s0) = make_float4(h[u][4], h[u][5], h[u][6], h[u][7]);
+                    if (p.y && unit < p.H) {
+                        float *yr = p.y + (long long)(t + p.T * unit) * p.ld_y + n0;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const int s = (j < 4 ? s0 + j : sh + s0 + j - 4);
+                            if (s < nval) yr[s] = h[u][j];
+                        }
+                    }
+                }
+            }
+            cp_async_wait_all();
+            __syncthreads();
+        }
+        if (active) {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int unit = u ? u1 : u0;
+                if (unit >= p.H) continue;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int s = (j < 4 ? s0 + j : sh + s0 + j - 4);
+                    if (s >= nval) continue;
+                    if (p.hn) p.hn[(long long)unit * p.ld_hn + n0 + s] = h[u][j];
+                    if (p.cn) p.cn[(long long)unit * p.ld_cn + n0 + s] = c[u][j];
+                }
+            }
+        }
+    }
+}
+
+// ---- conv + relu + pool --------------------------------------------------------
+__device__ __forceinline__ float conv_value(const ConvArgs &p, const float *in, int oc, int ch, int cw) {
+    if (!p.conv) return in[(long long)(oc + p.C * (ch + p.Hin * cw)) * p.ld_in];
+    const float *w = p.arena + p.w_off + (long long)oc * p.C * p.KS * p.KS;
+    float acc = 0.f;
+    for (int ic = 0; ic < p.C; ic++)
+        for (int kh = 0; kh < p.KS; kh++) {
+            const int ih = ch * p.str_h - p.pad_h + kh;
+            if (ih < 0 || ih >= p.Hin) continue;
+            for (int kw = 0; kw < p.KS; kw++) {
+                const int iw = cw * p.str_w - p.pad_w + kw;
+                if (iw < 0 || iw >= p.Win) continue;
+                acc = fmaf(__ldg(w + (ic * p.KS + kh) * p.KS + kw), in[(long long)(ic + p.C * (ih + p.Hin * iw)) * p.ld_in], acc);
+            }
+        }
+    acc += __ldg(p.arena + p.b_off + oc);
+    return p.relu ? (acc < 0.f ? 0.f : acc) : acc;
+}
+
+__global__ void __launch_bounds__(128) conv_pool_kernel(const ConvArgs p) {
+    const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= p.n) return;
+    const int e = blockIdx.y;  // pooled output element, oc fastest
+    const int oc = e % p.OC, rest = e / p.OC, ph = rest % p.Hq, pw = rest / p.Hq;
+    const float *in = p.in + s;
+    float v;
+    if (!p.pool) {
+        v = conv_value(p, in, oc, ph, pw);
+    } else {
+        float best = -INFINITY, sum = 0.f;
+        for (int dw = 0; dw < p.pk; dw++)
+            for (int dh = 0; dh < p.pk; dh++) {
+                const int ch = ph * p.pstr_h - p.ppad_h + dh, cw = pw * p.pstr_w - p.ppad_w + dw;
+                // the reference zero-pads the pooled array (layers.f90:134-181)
+                const float x = (ch < 0 || ch >= p.Ho || cw < 0 || cw >= p.Wo) ? 0.f : conv_value(p, in, oc, ch, cw);
+                best = fmaxf(best, x);
+                sum += x;
+            }
+        v = p.pool == 1 ? best : sum / (float)(p.pk * p.pk);
+    }
+    p.out[(long long)(oc * p.so_c + ph * p.so_h + pw * p.so_w) * p.ld_out + s] = v;
+}
+
+// ---- data movement / elementwise ------------------------------------------------
+__global__ void gather_kernel(const float *in, long long ld_in, float *out, long long ld_out, const int *map, long long n) {
+    const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const long long r = blockIdx.y;
+    const long long src = map ? map[r] : r;
+    out[r * ld_out + s] = in[src * ld_in + s];
+}
+
+__global__ void act_kernel(const float *in, long long ld_in, float *out, long long ld_out, long long n, int act) {
+    const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const long long r = blockIdx.y;
+    out[r * ld_out + s] = apply_act(in[r * ld_in + s], act);
+}
+
+}  // namespace
+
+size_t mlp_smem_bytes(const MlpLayerDev *L, int nl, int *S_out) {
+    int max_mp = 8, hid = 8, bias_total = 0;
+    for (int l = 0; l < nl; l++) {
+        max_mp = std::max(max_mp, L[l].Mp);
+        if (l + 1 < nl) hid = std::max(hid, L[l].Mp);
+        bias_total += L[l].Mp;
+    }
+    const int a_rows = std::min(kKC, L[0].Kp);
+    // every layer's product must fit one 8x8 tile per thread: (Mp/8)*(S/8) <= 256
+    for (int S = std::min(256, (16384 / max_mp) / 8 * 8); S >= 8; S -= 8) {
+        size_t bytes = sizeof(float) * ((size_t)2 * hid * S + (size_t)2 * kKC * max_mp + (size_t)2 * a_rows * S + bias_total);
+        if (bytes <= kMaxSmem) {
+            *S_out = S;
+            return bytes;
+        }
+    }
+    return 0;
+}
+
+size_t lstm_smem_bytes(int Ip, int Hp, int *S_out) {
+    const int K = Ip + Hp, G = 4 * Hp;
+    int Smax = std::min(256, (8 * kThreads / (Hp / 2)) / 8 * 8);
+    for (int S = Smax; S >= 8; S -= 8) {
+        size_t bytes = sizeof(float) * ((size_t)K * G + G + (size_t)2 * K * S);
+        if (bytes <= kMaxSmem) {
+            *S_out = S;
+            return bytes;
+        }
+    }
+    return 0;
+}
+
+cudaError_t configure_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(mlp_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(lstm_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+}
+
+cudaError_t launch_mlp(MlpArgs a, const MlpLayerDev *L, int num_sms, cudaStream_t st) {
+    int S = 0;
+    size_t bytes = mlp_smem_bytes(L, a.nlayers, &S);
+    if (!bytes) return cudaErrorInvalidConfiguration;
+    a.S = S;
+    a.max_mp = 8;
+    a.hid_rows = 8;
+    a.bias_total = 0;
+    for (int l = 0; l < a.nlayers; l++) {
+        a.max_mp = std::max(a.max_mp, L[l].Mp);
+        if (l + 1 < a.nlayers) a.hid_rows = std::max(a.hid_rows, L[l].Mp);
+        a.bias_total += L[l].Mp;
+    }
+    a.stage_a_rows = std::min(kKC, L[0].Kp);
+    const long long tiles = (a.n + S - 1) / S;
+    const int grid = (int)std::min<long long>(tiles, num_sms);
+    if (grid <= 0) return cudaSuccess;
+    mlp_ffma_kernel<<<grid, kThreads, bytes, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lstm(LstmArgs a, int num_sms, cudaStream_t st) {
+    int S = 0;
+    size_t bytes = lstm_smem_bytes(a.Ip, a.Hp, &S);
+    if (!bytes) return cudaErrorInvalidConfiguration;
+    a.S = S;
+    const long long tiles = (a.n + S - 1) / S;
+    const int grid = (int)std::min<long long>(tiles, num_sms);
+    if (grid <= 0) return cudaSuccess;
+    lstm_ffma_kernel<<<grid, kThreads, bytes, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
+    const long long outs = (long long)a.OC * a.Hq * a.Wq;
+    if (a.n <= 0 || outs <= 0) return cudaSuccess;
+    if (outs > 65535) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)((a.n + 127) / 128), (unsigned)outs);
+    conv_pool_kernel<<<grid, 128, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const float *in, long long ld_in, float *out, long long ld_out, const int *map, long long rows,
+                          long long n, cudaStream_t st) {
+    if (n <= 0 || rows <= 0) return cudaSuccess;
+    if (rows > 65535) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)((n + 255) / 256), (unsigned)rows);
+    gather_kernel<<<grid, 256, 0, st>>>(in, ld_in, out, ld_out, map, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_act(const float *in, long long ld_in, float *out, long long ld_out, long long rows, long long n,
+                       int act, cudaStream_t st) {
+    if (n <= 0 || rows <= 0) return cudaSuccess;
+    if (rows > 65535) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)((n + 255) / 256), (unsigned)rows);
+    act_kernel<<<grid, 256, 0, st>>>(in, ld_in, out, ld_out, n, act);
+    return cudaGetLastError();
+}
+
+}  // namespace rosenna

@@ -1,0 +1,708 @@
+// Builds the launch plan by interpreting variables.fpp's `architecture` list
+// the way fLibrary/modelCreator.fpp:79-171 expands it into Fortran calls:
+// one entry per ONNX node, operating on named allocatable arrays.  Instead of
+// emitting layer calls, each entry extends the plan:
+//   Gemm (+ Relu/Tanh/Sigmoid) chains      -> one fused MLP step
+//   LSTM                                   -> one persistent LSTM step
+//   Conv (+ Relu) (+ MaxPool/AveragePool)  -> one fused conv/pool step
+//   Transpose / Squeeze / Reshape          -> nothing when the per-sample element
+//                                             order is unchanged, else a gather
+// Data movement ops are evaluated with the reference's own index formulas
+// (Fortran RESHAPE with ORDER) at a probe batch of 3, which both checks that the
+// op keeps samples independent and yields the per-sample row map.
+#include "plan.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <set>
+#include <sstream>
+
+#include "../../include/rosenna.h"
+
+namespace rosenna {
+namespace {
+
+using Shape = std::vector<int64_t>;
+constexpr int64_t kProbe = 3;
+
+int64_t numel(const Shape &s) {
+    int64_t n = 1;
+    for (auto d : s) n *= d;
+    return n;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+std::string shape_str(const Shape &s) {
+    std::ostringstream o;
+    o << "(";
+    for (size_t i = 0; i < s.size(); i++) o << (i ? "," : "") << s[i];
+    o << ")";
+    return o.str();
+}
+
+void unravel(int64_t L, const Shape &s, int64_t *sub) {
+    for (size_t i = 0; i < s.size(); i++) {
+        sub[i] = L % s[i];
+        L /= s[i];
+    }
+}
+
+int64_t ravel(const int64_t *sub, const Shape &s) {
+    int64_t L = 0, st = 1;
+    for (size_t i = 0; i < s.size(); i++) {
+        L += sub[i] * st;
+        st *= s[i];
+    }
+    return L;
+}
+
+// Fortran RESHAPE(SOURCE, SHAPE=R, ORDER=order1): source elements in array
+// element order fill R with subscript order1(1) varying fastest.
+// Returns, for each element of R (column-major linear index), its source index.
+std::vector<int64_t> fortran_reshape_order_map(const Shape &src, const Shape &R, const std::vector<int64_t> &order1) {
+    std::vector<int64_t> m((size_t)numel(R), -1);
+    int64_t n = std::min(numel(src), numel(R));
+    std::vector<int64_t> stride(R.size()), sub(R.size(), 0);
+    int64_t st = 1;
+    for (size_t i = 0; i < R.size(); i++) {
+        stride[i] = st;
+        st *= R[i];
+    }
+    for (int64_t L = 0; L < n; L++) {
+        int64_t off = 0;
+        for (size_t k = 0; k < R.size(); k++) off += sub[order1[k] - 1] * stride[order1[k] - 1];
+        m[(size_t)off] = L;
+        for (size_t k = 0; k < R.size(); k++) {
+            int64_t d = order1[k] - 1;
+            if (++sub[d] < R[d]) break;
+            sub[d] = 0;
+        }
+    }
+    return m;
+}
+
+// C-order reshape (the two RESHAPEs of modelCreator.fpp:125-126 compose to it).
+std::vector<int64_t> c_order_reshape_map(const Shape &src, const Shape &R) {
+    std::vector<int64_t> m((size_t)numel(R), -1);
+    std::vector<int64_t> sr(R.size()), ss(src.size());
+    for (int64_t L = 0; L < numel(R); L++) {
+        unravel(L, R, sr.data());
+        int64_t c = 0;
+        for (size_t i = 0; i < R.size(); i++) c = c * R[i] + sr[i];
+        for (size_t i = src.size(); i-- > 0;) {
+            ss[i] = c % src[i];
+            c /= src[i];
+        }
+        m[(size_t)L] = ravel(ss.data(), src);
+    }
+    return m;
+}
+
+// From a full index map at the probe batch, derive the per-sample row map.
+bool per_sample_map(const Shape &S, int b, const Shape &R, int b2, const std::vector<int64_t> &r2s,
+                    std::vector<int32_t> *map) {
+    int64_t rows_r = numel(R) / R[b2];
+    map->assign((size_t)rows_r, -1);
+    std::vector<int64_t> sr(R.size()), ss(S.size());
+    for (int64_t L = 0; L < numel(R); L++) {
+        int64_t Ls = r2s[(size_t)L];
+        if (Ls < 0) return false;
+        unravel(L, R, sr.data());
+        unravel(Ls, S, ss.data());
+        if (sr[b2] != ss[b]) return false;
+        int64_t pr = 0, st = 1;
+        for (size_t i = 0; i < R.size(); i++)
+            if ((int)i != b2) { pr += sr[i] * st; st *= R[i]; }
+        int64_t ps = 0;
+        st = 1;
+        for (size_t i = 0; i < S.size(); i++)
+            if ((int)i != b) { ps += ss[i] * st; st *= S[i]; }
+        int32_t &slot = (*map)[(size_t)pr];
+        if (slot == -1) slot = (int32_t)ps;
+        else if (slot != ps) return false;
+    }
+    for (auto v : *map)
+        if (v < 0) return false;
+    return true;
+}
+
+bool is_identity(const std::vector<int32_t> &m, int64_t src_rows) {
+    if ((int64_t)m.size() != src_rows) return false;
+    for (size_t i = 0; i < m.size(); i++)
+        if (m[i] != (int32_t)i) return false;
+    return true;
+}
+
+struct TVal {
+    Shape shape;
+    int bdim = 0;
+    int buf = -1;  // -2: value not representable per sample (an error if read)
+    int64_t rows() const { return numel(shape) / shape[(size_t)bdim]; }
+};
+
+class Builder {
+  public:
+    Builder(const ModelFiles &mf, Plan *plan) : mf_(mf), plan_(plan) {}
+    Status run();
+
+  private:
+    const ModelFiles &mf_;
+    Plan *plan_;
+    std::map<std::string, TVal> vars_;
+    std::vector<int> refc_;
+    int64_t B0_ = 1;
+    int n_gemm_ = 0, n_lstm_ = 0, n_conv_ = 0, n_max_ = 0, n_avg_ = 0;
+
+    int new_buf(int64_t rows) {
+        plan_->buf_rows.push_back(rows);
+        refc_.push_back(0);
+        return (int)plan_->buf_rows.size() - 1;
+    }
+    void bind(const std::string &name, const TVal &v) {
+        auto it = vars_.find(name);
+        if (it != vars_.end() && it->second.buf >= 0) refc_[(size_t)it->second.buf]--;
+        if (v.buf >= 0) refc_[(size_t)v.buf]++;
+        vars_[name] = v;
+    }
+    Status get(const std::string &name, TVal *v) {
+        auto it = vars_.find(name);
+        if (it == vars_.end()) return Status::Err(ROSENNA_ERR_FORMAT, "architecture reads undefined variable '" + name + "'");
+        if (it->second.buf < 0)
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED, "variable '" + name + "' mixes samples after a Reshape; not batched");
+        *v = it->second;
+        return Status::Ok();
+    }
+    int64_t put(const float *p, size_t n) {
+        auto &a = plan_->arena;
+        size_t off = (size_t)round_up((int64_t)a.size(), 4);
+        a.resize(off + n, 0.f);
+        if (n) std::memcpy(a.data() + off, p, n * sizeof(float));
+        a.resize((size_t)round_up((int64_t)a.size(), 4), 0.f);
+        return (int64_t)off;
+    }
+    int64_t put_map(const std::vector<int32_t> &m) {
+        static_assert(sizeof(int32_t) == sizeof(float), "map words");
+        return put(reinterpret_cast<const float *>(m.data()), m.size());
+    }
+    Step *last_producing(int buf) {
+        if (plan_->steps.empty()) return nullptr;
+        Step &s = plan_->steps.back();
+        if (s.out != buf || refc_[(size_t)buf] != 1) return nullptr;
+        return &s;
+    }
+    // data movement: bind `name` to `x` rearranged through a full-index map at the
+    // probe batch; `Rx` is the result shape at the export batch.
+    Status move(const std::string &name, const TVal &x, const Shape &Rx, const Shape &R, int b2,
+                const std::vector<int64_t> &r2s, const Shape &S, bool poison_on_fail) {
+        std::vector<int32_t> m;
+        TVal out{Rx, b2, -1};
+        if (!per_sample_map(S, x.bdim, R, b2, r2s, &m)) {
+            if (!poison_on_fail)
+                return Status::Err(ROSENNA_ERR_UNSUPPORTED, "a data-movement op on " + shape_str(x.shape) + " mixes samples");
+            out.buf = -2;
+            bind(name, out);
+            return Status::Ok();
+        }
+        if (is_identity(m, x.rows())) {
+            out.buf = x.buf;
+        } else {
+            Step s;
+            s.kind = Step::GATHER;
+            s.in = x.buf;
+            s.out = new_buf((int64_t)m.size());
+            s.map_off = put_map(m);
+            plan_->steps.push_back(s);
+            out.buf = s.out;
+        }
+        bind(name, out);
+        return Status::Ok();
+    }
+    Shape probe(const TVal &x) {
+        Shape S = x.shape;
+        S[(size_t)x.bdim] = kProbe;
+        return S;
+    }
+
+    Status op_gemm(const PyVal &e);
+    Status op_act(const PyVal &e, int act);
+    Status op_lstm(const PyVal &e);
+    Status op_conv(const PyVal &e);
+    Status op_pool(const PyVal &e, bool avg);
+    Status op_transpose(const PyVal &e);
+    Status op_reshape(const PyVal &e);
+    Status op_squeeze(const PyVal &e);
+    Status finish();
+};
+
+Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90:11-23
+    TVal x;
+    Status st = get(e.at(1).at(0).s, &x);
+    if (!st.ok()) return st;
+    int transB = (int)e.at(1).at(1).as_int();
+    if (n_gemm_ >= (int)mf_.lin.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more Gemm nodes than Gemm weights");
+    const LinearWeights &L = mf_.lin[(size_t)n_gemm_++];
+    if (transB != 1) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gemm with transB=0 (W.inp form) is not supported");
+    int rsub = 1;
+    if (x.shape.size() == 3 && x.bdim == 1) rsub = (int)x.shape[0];  // (r, batch, K): r sub-rows per sample
+    else if (x.shape.size() != 2 || x.bdim != 0)
+        return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gemm input must be (batch, K), got " + shape_str(x.shape));
+    int M = (int)L.w.dims[0], K = (int)L.w.dims[1];
+    if (x.shape.back() != K) return Status::Err(ROSENNA_ERR_SHAPE, "Gemm: input " + shape_str(x.shape) + " vs weights (" + std::to_string(M) + "," + std::to_string(K) + ")");
+    if ((int64_t)L.b.v.size() != M) return Status::Err(ROSENNA_ERR_FORMAT, "Gemm: bias size");
+    MlpLayer ly;
+    ly.K = K;
+    ly.M = M;
+    ly.Kp = (int)round_up(K, 8);
+    ly.Mp = (int)round_up(M, 8);
+    std::vector<float> wt((size_t)ly.Kp * ly.Mp, 0.f), b((size_t)ly.Mp, 0.f);
+    for (int k = 0; k < K; k++)
+        for (int m = 0; m < M; m++) wt[(size_t)k * ly.Mp + m] = (float)L.w.v[(size_t)m + (size_t)M * k];
+    for (int m = 0; m < M; m++) b[(size_t)m] = (float)L.b.v[(size_t)m];
+    ly.w_off = put(wt.data(), wt.size());
+    ly.b_off = put(b.data(), b.size());
+    Step *prev = last_producing(x.buf);
+    int out;
+    if (prev && prev->kind == Step::MLP && prev->rsub == rsub) {
+        prev->layers.push_back(ly);
+        out = prev->out;
+    } else {
+        Step s;
+        s.kind = Step::MLP;
+        s.in = x.buf;
+        s.out = out = new_buf((int64_t)rsub * M);
+        s.rsub = rsub;
+        s.layers.push_back(ly);
+        plan_->steps.push_back(s);
+    }
+    plan_->buf_rows[(size_t)out] = (int64_t)rsub * M;
+    Shape os = x.shape;
+    os.back() = M;
+    bind(e.at(1).at(0).s, TVal{os, x.bdim, out});
+    return Status::Ok();
+}
+
+Status Builder::op_act(const PyVal &e, int act) {  // modelCreator.fpp:151-161
+    const std::string &name = e.at(1).at(0).s;
+    TVal x;
+    Status st = get(name, &x);
+    if (!st.ok()) return st;
+    Step *prev = last_producing(x.buf);
+    if (prev && prev->kind == Step::MLP && prev->layers.back().act == ACT_NONE) {
+        prev->layers.back().act = act;
+        return Status::Ok();
+    }
+    if (prev && prev->kind == Step::CONV && prev->conv && !prev->relu && prev->pool == 0 && act == ACT_RELU) {
+        prev->relu = true;
+        return Status::Ok();
+    }
+    Step s;
+    s.kind = Step::ACT;
+    s.act = act;
+    s.in = x.buf;
+    s.out = new_buf(x.rows());
+    plan_->steps.push_back(s);
+    x.buf = s.out;
+    bind(name, x);
+    return Status::Ok();
+}
+
+Status Builder::op_lstm(const PyVal &e) {  // modelCreator.fpp:92-100, layers.f90:62-132
+    const std::string &xn = e.at(1).at(0).s, &hn = e.at(1).at(1).s, &cn = e.at(1).at(2).s;
+    const std::string &yn = e.at(2).at(0).s;
+    int flag = (int)e.at(e.size() - 1).at(0).as_int();
+    if (n_lstm_ >= (int)mf_.lstm.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more LSTM nodes than LSTM weights");
+    const LstmWeights &L = mf_.lstm[(size_t)n_lstm_++];
+    TVal x;
+    Status st = get(xn, &x);
+    if (!st.ok()) return st;
+    if (x.shape.size() != 3 || x.bdim != 1)
+        return Status::Err(ROSENNA_ERR_UNSUPPORTED, "LSTM input must be (T, batch, I), got " + shape_str(x.shape));
+    int T = (int)x.shape[0], I = (int)x.shape[2];
+    if (L.wih.dims.size() != 3 || L.wih.dims[1] % 4) return Status::Err(ROSENNA_ERR_FORMAT, "LSTM weights");
+    int H = (int)(L.wih.dims[1] / 4);
+    if (L.wih.dims[2] != I || L.whh.dims[1] != 4 * H || L.whh.dims[2] != H || (int64_t)L.bih.v.size() != 4 * H ||
+        (int64_t)L.bhh.v.size() != 4 * H)
+        return Status::Err(ROSENNA_ERR_SHAPE, "LSTM weight shapes do not match input " + shape_str(x.shape));
+    Step s;
+    s.kind = Step::LSTM;
+    s.in = x.buf;
+    s.T = T;
+    s.I = I;
+    s.H = H;
+    s.Ip = (int)round_up(I, 4);
+    s.Hp = (int)round_up(H, 2);
+    if (flag == 0) {
+        TVal h, c;
+        if (!(st = get(hn, &h)).ok() || !(st = get(cn, &c)).ok()) return st;
+        if (h.rows() != H || c.rows() != H || h.bdim != 1 || c.bdim != 1)
+            return Status::Err(ROSENNA_ERR_SHAPE, "LSTM state must be (1, batch, H)");
+        s.h0 = h.buf;
+        s.c0 = c.buf;
+    } else {  // constant initial state from the weights file (modelParserONNX.py:210-226 writes zeros)
+        auto constant = [&](const HostArray &a, int64_t *off) -> Status {
+            bool zero = true;
+            for (double v : a.v) zero = zero && v == 0.0;
+            if (zero) return Status::Ok();
+            if (a.dims.size() != 3 || a.dims[1] != 1 || a.dims[2] != H)
+                return Status::Err(ROSENNA_ERR_UNSUPPORTED, "non-zero constant LSTM state exported at batch > 1");
+            std::vector<float> v((size_t)s.Hp, 0.f);
+            for (int j = 0; j < H; j++) v[(size_t)j] = (float)a.v[(size_t)j];
+            *off = put(v.data(), v.size());
+            return Status::Ok();
+        };
+        if (!(st = constant(L.hid, &s.h0_const)).ok() || !(st = constant(L.cell, &s.c0_const)).ok()) return st;
+    }
+    // W = [Wih | Whh]^T with gate columns interleaved per unit: column 4j+q is
+    // gate q (i, f, g, o; layers.f90:88-93) of unit j, i.e. PyTorch row q*H+j.
+    int G = 4 * s.Hp, Kr = s.Ip + s.Hp;
+    std::vector<float> wt((size_t)Kr * G, 0.f), bias((size_t)G, 0.f);
+    for (int j = 0; j < H; j++)
+        for (int q = 0; q < 4; q++) {
+            int col = 4 * j + q, r = q * H + j;
+            for (int k = 0; k < I; k++) wt[(size_t)k * G + col] = (float)L.wih.v[(size_t)r + (size_t)4 * H * k];
+            for (int k = 0; k < H; k++) wt[(size_t)(s.Ip + k) * G + col] = (float)L.whh.v[(size_t)r + (size_t)4 * H * k];
+            bias[(size_t)col] = (float)(L.bih.v[(size_t)r] + L.bhh.v[(size_t)r]);
+        }
+    s.w_off = put(wt.data(), wt.size());
+    s.b_off = put(bias.data(), bias.size());
+    s.y = new_buf((int64_t)T * H);
+    s.hn = new_buf(H);
+    s.cn = new_buf(H);
+    plan_->steps.push_back(s);
+    int64_t N = x.shape[1];
+    bind(yn, TVal{{T, 1, N, H}, 2, s.y});
+    bind(hn, TVal{{1, N, H}, 1, s.hn});
+    bind(cn, TVal{{1, N, H}, 1, s.cn});
+    return Status::Ok();
+}
+
+Status Builder::op_conv(const PyVal &e) {  // modelCreator.fpp:103-105, layers.f90:183-233
+    const std::string &name = e.at(1).at(0).s;
+    TVal x;
+    Status st = get(name, &x);
+    if (!st.ok()) return st;
+    if (n_conv_ >= (int)mf_.conv.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more Conv nodes than Conv weights");
+    const ConvWeights &W = mf_.conv[(size_t)n_conv_++];
+    if (x.shape.size() != 4 || x.bdim != 0) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Conv input must be (batch, C, H, W)");
+    auto pads = e.at(2).at(2).ints(), strides = e.at(2).at(3).ints();
+    if (pads.size() < 2 || strides.size() < 2) return Status::Err(ROSENNA_ERR_FORMAT, "Conv pads/strides");
+    Step s;
+    s.kind = Step::CONV;
+    s.conv = true;
+    s.C = (int)x.shape[1];
+    s.Hin = (int)x.shape[2];
+    s.Win = (int)x.shape[3];
+    s.OC = (int)W.w.dims[0];
+    s.KS = (int)W.w.dims[2];
+    if (W.w.dims[1] != s.C) return Status::Err(ROSENNA_ERR_SHAPE, "Conv channels");
+    if (W.w.dims[3] != s.KS) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "non-square Conv kernel (the reference assumes square)");
+    s.pad_h = (int)pads[0];
+    s.pad_w = (int)pads[1];
+    s.str_h = (int)strides[0];
+    s.str_w = (int)strides[1];
+    s.Ho = (s.Hin + 2 * s.pad_h - s.KS) / s.str_h + 1;
+    s.Wo = (s.Win + 2 * s.pad_w - s.KS) / s.str_w + 1;
+    if (s.Ho < 1 || s.Wo < 1 || s.str_h < 1 || s.str_w < 1) return Status::Err(ROSENNA_ERR_SHAPE, "Conv output is empty");
+    s.Hq = s.Ho;
+    s.Wq = s.Wo;
+    std::vector<float> w((size_t)s.OC * s.C * s.KS * s.KS), b((size_t)s.OC);
+    for (int oc = 0; oc < s.OC; oc++)
+        for (int ic = 0; ic < s.C; ic++)
+            for (int kh = 0; kh < s.KS; kh++)
+                for (int kw = 0; kw < s.KS; kw++)
+                    w[(((size_t)oc * s.C + ic) * s.KS + kh) * s.KS + kw] =
+                        (float)W.w.v[(size_t)oc + (size_t)s.OC * (ic + (size_t)s.C * (kh + (size_t)s.KS * kw))];
+    for (int oc = 0; oc < s.OC; oc++) b[(size_t)oc] = (float)W.b.v[(size_t)oc];
+    s.w_off = put(w.data(), w.size());
+    s.b_off = put(b.data(), b.size());
+    s.in = x.buf;
+    s.out = new_buf((int64_t)s.OC * s.Ho * s.Wo);
+    s.so_c = 1;
+    s.so_h = s.OC;
+    s.so_w = (int64_t)s.OC * s.Ho;
+    plan_->steps.push_back(s);
+    bind(name, TVal{{x.shape[0], s.OC, s.Ho, s.Wo}, 0, s.out});
+    return Status::Ok();
+}
+
+Status Builder::op_pool(const PyVal &e, bool avg) {  // modelCreator.fpp:107-114, layers.f90:236-310
+    const std::string &name = e.at(1).at(0).s;
+    TVal x;
+    Status st = get(name, &x);
+    if (!st.ok()) return st;
+    int &ctr = avg ? n_avg_ : n_max_;
+    const std::vector<int> &ks = avg ? mf_.avgpool : mf_.maxpool;
+    if (ctr >= (int)ks.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more pool nodes than pool layers");
+    int k = ks[(size_t)ctr++];
+    if (x.shape.size() != 4 || x.bdim != 0) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "pool input must be (batch, C, H, W)");
+    auto pads = e.at(2).at(1).ints(), strides = e.at(2).at(2).ints();
+    if (pads.size() < 2 || strides.size() < 2) return Status::Err(ROSENNA_ERR_FORMAT, "pool pads/strides");
+    int C = (int)x.shape[1], H = (int)x.shape[2], W = (int)x.shape[3];
+    int Hq = (H + 2 * (int)pads[0] - k) / (int)strides[0] + 1, Wq = (W + 2 * (int)pads[1] - k) / (int)strides[1] + 1;
+    if (Hq < 1 || Wq < 1) return Status::Err(ROSENNA_ERR_SHAPE, "pool output is empty");
+    if (Hq != Wq)
+        return Status::Err(ROSENNA_ERR_UNSUPPORTED,
+                           "pooling with a non-square output (the reference writes its columns with MODULO(.,rows))");
+    Step *prev = last_producing(x.buf);
+    Step *s;
+    if (prev && prev->kind == Step::CONV && prev->conv && prev->pool == 0) {
+        s = prev;
+    } else {
+        Step n;
+        n.kind = Step::CONV;
+        n.conv = false;
+        n.C = n.OC = C;
+        n.Hin = n.Ho = H;
+        n.Win = n.Wo = W;
+        n.in = x.buf;
+        n.out = new_buf(1);
+        plan_->steps.push_back(n);
+        s = &plan_->steps.back();
+    }
+    s->pool = avg ? 2 : 1;
+    s->pk = k;
+    s->ppad_h = (int)pads[0];
+    s->ppad_w = (int)pads[1];
+    s->pstr_h = (int)strides[0];
+    s->pstr_w = (int)strides[1];
+    s->Hq = Hq;
+    s->Wq = Wq;
+    s->so_c = 1;
+    s->so_h = C;
+    s->so_w = (int64_t)C * Hq;
+    plan_->buf_rows[(size_t)s->out] = (int64_t)C * Hq * Wq;
+    bind(name, TVal{{x.shape[0], C, Hq, Wq}, 0, s->out});
+    return Status::Ok();
+}
+
+Status Builder::op_transpose(const PyVal &e) {  // modelCreator.fpp:117-119
+    const std::string &name = e.at(1).at(0).s;
+    TVal x;
+    Status st = get(name, &x);
+    if (!st.ok()) return st;
+    auto order = e.at(2).at(0).ints();
+    if (order.size() != x.shape.size()) return Status::Err(ROSENNA_ERR_FORMAT, "Transpose order rank");
+    Shape S = probe(x), R(order.size()), Rx(order.size());
+    int b2 = -1;
+    for (size_t i = 0; i < order.size(); i++) {
+        if (order[i] < 1 || order[i] > (int64_t)order.size()) return Status::Err(ROSENNA_ERR_FORMAT, "Transpose order");
+        R[i] = S[(size_t)order[i] - 1];
+        Rx[i] = x.shape[(size_t)order[i] - 1];
+        if (order[i] - 1 == x.bdim) b2 = (int)i;
+    }
+    return move(name, x, Rx, R, b2, fortran_reshape_order_map(S, R, order), S, false);
+}
+
+Status Builder::op_reshape(const PyVal &e) {  // modelCreator.fpp:122-130
+    const std::string &xn = e.at(1).at(0).s;
+    const std::string &on = e.at(2).at(0).s;
+    int flag = (int)e.at(e.size() - 1).at(0).as_int();
+    if (flag != 0) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Reshape of a stored constant is not supported");
+    TVal x;
+    Status st = get(xn, &x);
+    if (!st.ok()) return st;
+    Shape tgt = e.at(3).at(0).ints();
+    if (tgt.empty() || numel(tgt) != numel(x.shape)) return Status::Err(ROSENNA_ERR_SHAPE, "Reshape size mismatch");
+    if (tgt[0] % B0_) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Reshape target does not lead with the batch");
+    Shape S = probe(x);
+    // out = C-order reshape of x.  A target whose first dim is r*batch (r > 1)
+    // keeps r sub-rows per sample: it is held as (r, batch, ...) with the batch
+    // second, which has the same column-major element order.
+    int64_t r = tgt[0] / B0_;
+    Shape Tfull = tgt, Tx, Tp;
+    Tfull[0] = r * kProbe;
+    int b2;
+    if (r == 1) {
+        Tx = tgt;
+        Tp = Tfull;
+        b2 = 0;
+    } else {
+        Tx = {r, B0_};
+        Tp = {r, kProbe};
+        Tx.insert(Tx.end(), tgt.begin() + 1, tgt.end());
+        Tp.insert(Tp.end(), tgt.begin() + 1, tgt.end());
+        b2 = 1;
+    }
+    TVal ox = x;
+    if (!(st = move(on, x, Tx, Tp, b2, c_order_reshape_map(S, Tfull), S, false)).ok()) return st;
+    // side effect of modelCreator.fpp:125: x itself is left with its axes reversed
+    int rk = (int)x.shape.size();
+    Shape Rv(x.shape.rbegin(), x.shape.rend()), Rp(S.rbegin(), S.rend());
+    std::vector<int64_t> ord((size_t)rk);
+    for (int i = 0; i < rk; i++) ord[(size_t)i] = rk - i;
+    return move(xn, ox, Rv, Rp, rk - 1 - x.bdim, fortran_reshape_order_map(S, Rp, ord), S, true);
+}
+
+Status Builder::op_squeeze(const PyVal &e) {  // modelCreator.fpp:133-135
+    const std::string &xn = e.at(1).at(0).s;
+    const std::string &on = e.at(2).at(0).s;
+    TVal x;
+    Status st = get(xn, &x);
+    if (!st.ok()) return st;
+    auto axes = e.at(3).at(0).ints();
+    Shape R;
+    int b2 = x.bdim;
+    for (int i = 0; i < (int)x.shape.size(); i++) {
+        bool sq = std::find(axes.begin(), axes.end(), (int64_t)i) != axes.end();
+        if (!sq) { R.push_back(x.shape[(size_t)i]); continue; }
+        if (i == x.bdim) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Squeeze of the batch dimension");
+        if (x.shape[(size_t)i] != 1) return Status::Err(ROSENNA_ERR_SHAPE, "Squeeze of a non-unit dimension");
+        if (i < x.bdim) b2--;
+    }
+    bind(on, TVal{R, b2, x.buf});  // same element order: no data movement
+    return Status::Ok();
+}
+
+Status Builder::finish() {
+    const ModelFiles &m = mf_;
+    // outputs: o<index> = outputs[<index>-th key]  (modelCreator.fpp:169-171)
+    std::set<int> used;
+    for (auto &io : plan_->inputs) used.insert(io.buf);
+    for (size_t i = 0; i < m.out_shape.size(); i++) {
+        if (i >= m.outputs.items.size()) return Status::Err(ROSENNA_ERR_FORMAT, "outputs dict shorter than outShape");
+        TVal v;
+        Status st = get(m.outputs.items[i].s, &v);
+        if (!st.ok()) return st;
+        IoDesc d;
+        d.shape = m.out_shape.at(i).at(1).ints();
+        if (numel(d.shape) != numel(v.shape))
+            return Status::Err(ROSENNA_ERR_SHAPE, "output " + std::to_string(i) + " size differs from outShape");
+        d.pre = 1;
+        for (int k = 0; k < v.bdim; k++) d.pre *= v.shape[(size_t)k];
+        d.bdim = v.bdim;
+        d.rows = v.rows();
+        d.buf = v.buf;
+        if (used.count(d.buf)) {  // an input (or another output) would be aliased: copy
+            Step s;
+            s.kind = Step::COPY;
+            s.in = d.buf;
+            s.out = d.buf = new_buf(d.rows);
+            plan_->steps.push_back(s);
+        }
+        used.insert(d.buf);
+        plan_->outputs.push_back(d);
+    }
+    // drop steps whose results nobody reads
+    std::set<int> live;
+    for (auto &o : plan_->outputs) live.insert(o.buf);
+    std::vector<Step> kept;
+    for (size_t i = plan_->steps.size(); i-- > 0;) {
+        Step s = plan_->steps[i];
+        bool alive;
+        if (s.kind == Step::LSTM) {
+            if (!live.count(s.y)) s.y = -1;
+            if (!live.count(s.hn)) s.hn = -1;
+            if (!live.count(s.cn)) s.cn = -1;
+            alive = s.y >= 0 || s.hn >= 0 || s.cn >= 0;
+        } else {
+            alive = live.count(s.out) > 0;
+        }
+        if (!alive) continue;
+        live.insert(s.in);
+        if (s.h0 >= 0) live.insert(s.h0);
+        if (s.c0 >= 0) live.insert(s.c0);
+        kept.push_back(s);
+    }
+    std::reverse(kept.begin(), kept.end());
+    plan_->steps = kept;
+    return Status::Ok();
+}
+
+Status Builder::run() {
+    const PyVal &arch = mf_.architecture;
+    // batch dimension of each model input: 1 when the first entry that reads it
+    // is an LSTM (X is (T,N,I), h/c are (1,N,H)), else 0
+    std::set<std::string> lstm_operands, seen;
+    for (auto &e : arch.items) {
+        std::vector<std::string> names;
+        const PyVal &a1 = e.at(1);
+        if (a1.is_list()) {
+            for (auto &n : a1.items)
+                if (n.kind == PyVal::STR) names.push_back(n.s);
+        }
+        for (auto &n : names) {
+            if (seen.count(n)) continue;
+            seen.insert(n);
+            if (e.at(0).s == "LSTM") lstm_operands.insert(n);
+        }
+    }
+    for (size_t i = 0; i < mf_.true_inputs.size(); i++) {
+        const PyVal &ti = mf_.true_inputs.at(i);
+        IoDesc d;
+        d.shape = ti.at(1).ints();
+        if (d.shape.empty()) return Status::Err(ROSENNA_ERR_FORMAT, "input without shape");
+        d.bdim = lstm_operands.count(ti.at(0).s) && d.shape.size() >= 2 ? 1 : 0;
+        int64_t b = d.shape[(size_t)d.bdim];
+        if (i == 0) B0_ = b;
+        else if (b != B0_) return Status::Err(ROSENNA_ERR_SHAPE, "inputs disagree on the export batch size");
+        for (int k = 0; k < d.bdim; k++)
+            if (d.shape[(size_t)k] != 1) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "input with non-unit dims in front of its batch dimension");
+        d.rows = numel(d.shape) / b;
+        d.buf = new_buf(d.rows);
+        plan_->inputs.push_back(d);
+        bind(ti.at(0).s, TVal{d.shape, d.bdim, d.buf});
+    }
+    plan_->export_batch = B0_;
+    for (auto &e : arch.items) {
+        const std::string &op = e.at(0).s;
+        Status st;
+        if (op == "Gemm") st = op_gemm(e);
+        else if (op == "Relu") st = op_act(e, ACT_RELU);
+        else if (op == "Tanh") st = op_act(e, ACT_TANH);
+        else if (op == "Sigmoid") st = op_act(e, ACT_SIGMOID);
+        else if (op == "LSTM") st = op_lstm(e);
+        else if (op == "Conv") st = op_conv(e);
+        else if (op == "MaxPool") st = op_pool(e, false);
+        else if (op == "AveragePool") st = op_pool(e, true);
+        else if (op == "Transpose") st = op_transpose(e);
+        else if (op == "Reshape") st = op_reshape(e);
+        else if (op == "Squeeze") st = op_squeeze(e);
+        else st = Status::Err(ROSENNA_ERR_UNSUPPORTED, "op " + op + " is not supported by the engine");
+        if (!st.ok()) return st;
+    }
+    return finish();
+}
+
+}  // namespace
+
+Status build_plan(const ModelFiles &mf, Plan *plan) {
+    *plan = Plan();
+    Builder b(mf, plan);
+    return b.run();
+}
+
+std::string Plan::describe() const {
+    std::ostringstream o;
+    static const char *acts[] = {"", "relu", "tanh", "sigmoid"};
+    for (auto &s : steps) {
+        switch (s.kind) {
+            case Step::MLP:
+                o << "mlp b" << s.in << "->b" << s.out << " [";
+                for (size_t i = 0; i < s.layers.size(); i++)
+                    o << (i ? " " : "") << s.layers[i].K << "x" << s.layers[i].M << (s.layers[i].act ? ":" : "")
+                      << acts[s.layers[i].act];
+                o << "]\n";
+                break;
+            case Step::LSTM:
+                o << "lstm b" << s.in << " T=" << s.T << " I=" << s.I << " H=" << s.H << " h0=b" << s.h0 << " c0=b"
+                  << s.c0 << " -> y=b" << s.y << " hn=b" << s.hn << " cn=b" << s.cn << "\n";
+                break;
+            case Step::CONV:
+                o << (s.conv ? "conv" : "pool") << " b" << s.in << "->b" << s.out << " C=" << s.C << " " << s.Hin << "x"
+                  << s.Win;
+                if (s.conv) o << " OC=" << s.OC << " k=" << s.KS << " pad=" << s.pad_h << "," << s.pad_w << " s=" << s.str_h << "," << s.str_w;
+                if (s.relu) o << " relu";
+                if (s.pool) o << (s.pool == 1 ? " maxpool" : " avgpool") << " k=" << s.pk << " s=" << s.pstr_h;
+                o << " -> " << s.Hq << "x" << s.Wq << "\n";
+                break;
+            case Step::GATHER: o << "gather b" << s.in << "->b" << s.out << "\n"; break;
+            case Step::ACT: o << "act:" << acts[s.act] << " b" << s.in << "->b" << s.out << "\n"; break;
+            case Step::COPY: o << "copy b" << s.in << "->b" << s.out << "\n"; break;
+        }
+    }
+    return o.str();
+}
+
+}  // namespace rosenna

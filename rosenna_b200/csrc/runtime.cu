@@ -1,0 +1,573 @@
+// C ABI of the engine: initialize / use_model and friends (include/rosenna.h).
+//
+// initialize() reads the three model files, builds the launch plan and uploads
+// the packed weights to every selected GPU.  use_model splits the batch into
+// contiguous sample ranges, one per GPU (one host thread each), and runs the
+// plan on chunks of samples: host->device copies of a chunk's rows, the plan's
+// kernels, device->host copies, with two streams alternating chunks so that the
+// copies of one chunk overlap the kernels of the other.  No collective is
+// involved: samples are independent and weights are replicated.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/rosenna.h"
+#include "kernels.cuh"
+#include "model_files.hpp"
+#include "plan.hpp"
+
+namespace rosenna {
+namespace {
+
+constexpr int kSlots = 2;
+
+struct Slot {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;     // last device-path use of this slot's scratch
+    int64_t cap = 0;                // samples the scratch buffers hold
+    std::vector<float *> scratch;   // per plan buffer (intermediates only)
+    std::vector<float *> io;        // per plan buffer: device copies of inputs/outputs (host path)
+    int64_t io_cap = 0;
+};
+
+struct Device {
+    int id = 0;
+    int num_sms = 148;
+    float *arena = nullptr;
+    Slot slots[kSlots];
+};
+
+struct Context {
+    bool ready = false;
+    ModelFiles mf;
+    Plan plan;
+    std::string desc;
+    std::vector<int> device_ids;  // selected by rosenna_set_devices (empty: all)
+    std::vector<std::unique_ptr<Device>> devs;
+    std::vector<MlpLayerDev> mlp_tables;       // host copies, concatenated
+    std::vector<int64_t> mlp_table_off;        // per step: index into mlp_tables, device offset in arena
+    std::vector<int64_t> mlp_table_arena_off;
+    std::vector<bool> is_io_in, is_io_out;
+};
+
+Context g_ctx;
+std::mutex g_mu;
+int g_status = 0;
+std::string g_error;
+std::atomic<int64_t> g_launches{0};
+
+int fail(int code, const std::string &msg) {
+    g_status = code;
+    g_error = msg;
+    return code;
+}
+int ok() {
+    g_status = 0;
+    g_error.clear();
+    return 0;
+}
+
+#define CUDA_TRY(expr)                                                                                         \
+    do {                                                                                                       \
+        cudaError_t e_ = (expr);                                                                               \
+        if (e_ != cudaSuccess)                                                                                 \
+            return Status::Err(ROSENNA_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));          \
+    } while (0)
+
+int64_t scratch_budget_bytes() {
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return (int64_t)4 << 30;
+    return (int64_t)std::min<size_t>(free_b / 4, (size_t)16 << 30);
+}
+
+void release_device(Device &d) {
+    cudaSetDevice(d.id);
+    for (auto &s : d.slots) {
+        for (auto p : s.scratch) cudaFree(p);
+        for (auto p : s.io) cudaFree(p);
+        s.scratch.clear();
+        s.io.clear();
+        s.cap = s.io_cap = 0;
+        if (s.stream) cudaStreamDestroy(s.stream);
+        if (s.done) cudaEventDestroy(s.done);
+        s.stream = nullptr;
+        s.done = nullptr;
+    }
+    cudaFree(d.arena);
+    d.arena = nullptr;
+}
+
+void release_all() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (auto &d : g_ctx.devs) release_device(*d);
+    g_ctx.devs.clear();
+    g_ctx.ready = false;
+    cudaSetDevice(cur);
+}
+
+// intermediate buffers: used by a step and not a model input/output
+bool is_scratch(int b) { return !g_ctx.is_io_in[(size_t)b] && !g_ctx.is_io_out[(size_t)b]; }
+
+Status ensure_scratch(Slot &s, int64_t cap) {
+    if (s.cap >= cap) return Status::Ok();
+    for (auto p : s.scratch) cudaFree(p);
+    s.scratch.assign(g_ctx.plan.buf_rows.size(), nullptr);
+    s.cap = 0;
+    std::vector<bool> used(g_ctx.plan.buf_rows.size(), false);
+    for (auto &st : g_ctx.plan.steps)
+        for (int b : {st.in, st.out, st.h0, st.c0, st.y, st.hn, st.cn})
+            if (b >= 0) used[(size_t)b] = true;
+    for (size_t b = 0; b < used.size(); b++) {
+        if (!used[b] || !is_scratch((int)b)) continue;
+        CUDA_TRY(cudaMalloc(&s.scratch[b], sizeof(float) * (size_t)g_ctx.plan.buf_rows[b] * (size_t)cap));
+    }
+    s.cap = cap;
+    return Status::Ok();
+}
+
+Status ensure_io(Slot &s, int64_t cap) {
+    if (s.io_cap >= cap) return Status::Ok();
+    for (auto p : s.io) cudaFree(p);
+    s.io.assign(g_ctx.plan.buf_rows.size(), nullptr);
+    s.io_cap = 0;
+    for (auto *v : {&g_ctx.plan.inputs, &g_ctx.plan.outputs})
+        for (auto &io : *v)
+            CUDA_TRY(cudaMalloc(&s.io[(size_t)io.buf], sizeof(float) * (size_t)io.rows * (size_t)cap));
+    s.io_cap = cap;
+    return Status::Ok();
+}
+
+// Largest chunk whose intermediates fit the scratch budget.
+int64_t max_chunk(int64_t n) {
+    int64_t rows = 0;
+    for (size_t b = 0; b < g_ctx.plan.buf_rows.size(); b++)
+        if (is_scratch((int)b)) rows += g_ctx.plan.buf_rows[b];
+    int64_t cap = n;
+    if (rows > 0) cap = std::max<int64_t>(1024, scratch_budget_bytes() / (int64_t)(sizeof(float) * rows));
+    return std::max<int64_t>(1, std::min(cap, n));
+}
+
+// Runs the plan on `cnt` samples.  ptr[b]/ld[b] address buffer b (row r of
+// sample s at ptr[b][r*ld[b] + s]).
+Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<int64_t> &ld, int64_t cnt,
+                cudaStream_t stream) {
+    const Plan &P = g_ctx.plan;
+    const float *arena = d.arena;
+    int64_t launches = 0;
+    for (size_t si = 0; si < P.steps.size(); si++) {
+        const Step &s = P.steps[si];
+        cudaError_t e = cudaSuccess;
+        switch (s.kind) {
+            case Step::MLP: {
+                MlpArgs a{};
+                a.arena = arena;
+                a.layers = reinterpret_cast<const MlpLayerDev *>(arena + g_ctx.mlp_table_arena_off[si]);
+                a.nlayers = (int)s.layers.size();
+                const MlpLayerDev *host_layers = g_ctx.mlp_tables.data() + g_ctx.mlp_table_off[si];
+                for (int t = 0; t < s.rsub; t++) {  // sub-row t: rows t + rsub*k
+                    a.in = ptr[(size_t)s.in] + (int64_t)t * ld[(size_t)s.in];
+                    a.ld_in = (int64_t)s.rsub * ld[(size_t)s.in];
+                    a.out = ptr[(size_t)s.out] + (int64_t)t * ld[(size_t)s.out];
+                    a.ld_out = (int64_t)s.rsub * ld[(size_t)s.out];
+                    a.n = cnt;
+                    e = launch_mlp(a, host_layers, d.num_sms, stream);
+                    launches++;
+                    if (e != cudaSuccess) break;
+                }
+                break;
+            }
+            case Step::LSTM: {
+                LstmArgs a{};
+                a.arena = arena;
+                a.w_off = s.w_off;
+                a.b_off = s.b_off;
+                a.h0_const = s.h0_const;
+                a.c0_const = s.c0_const;
+                a.x = ptr[(size_t)s.in];
+                a.ld_x = ld[(size_t)s.in];
+                if (s.h0 >= 0) { a.h0 = ptr[(size_t)s.h0]; a.ld_h0 = ld[(size_t)s.h0]; }
+                if (s.c0 >= 0) { a.c0 = ptr[(size_t)s.c0]; a.ld_c0 = ld[(size_t)s.c0]; }
+                if (s.y >= 0) { a.y = ptr[(size_t)s.y]; a.ld_y = ld[(size_t)s.y]; }
+                if (s.hn >= 0) { a.hn = ptr[(size_t)s.hn]; a.ld_hn = ld[(size_t)s.hn]; }
+                if (s.cn >= 0) { a.cn = ptr[(size_t)s.cn]; a.ld_cn = ld[(size_t)s.cn]; }
+                a.n = cnt;
+                a.T = s.T;
+                a.I = s.I;
+                a.H = s.H;
+                a.Ip = s.Ip;
+                a.Hp = s.Hp;
+                e = launch_lstm(a, d.num_sms, stream);
+                launches++;
+                break;
+            }
+            case Step::CONV: {
+                ConvArgs a{};
+                a.arena = arena;
+                a.w_off = s.w_off;
+                a.b_off = s.b_off;
+                a.in = ptr[(size_t)s.in];
+                a.ld_in = ld[(size_t)s.in];
+                a.out = ptr[(size_t)s.out];
+                a.ld_out = ld[(size_t)s.out];
+                a.n = cnt;
+                a.conv = s.conv;
+                a.relu = s.relu;
+                a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.OC = s.OC; a.KS = s.KS;
+                a.pad_h = s.pad_h; a.pad_w = s.pad_w; a.str_h = s.str_h; a.str_w = s.str_w;
+                a.Ho = s.Ho; a.Wo = s.Wo;
+                a.pool = s.pool; a.pk = s.pk; a.ppad_h = s.ppad_h; a.ppad_w = s.ppad_w;
+                a.pstr_h = s.pstr_h; a.pstr_w = s.pstr_w; a.Hq = s.Hq; a.Wq = s.Wq;
+                a.so_c = s.so_c; a.so_h = s.so_h; a.so_w = s.so_w;
+                e = launch_conv(a, stream);
+                launches++;
+                break;
+            }
+            case Step::GATHER:
+            case Step::COPY: {
+                const int *map = s.kind == Step::GATHER ? reinterpret_cast<const int *>(arena + s.map_off) : nullptr;
+                e = launch_gather(ptr[(size_t)s.in], ld[(size_t)s.in], ptr[(size_t)s.out], ld[(size_t)s.out], map,
+                                  P.buf_rows[(size_t)s.out], cnt, stream);
+                launches++;
+                break;
+            }
+            case Step::ACT:
+                e = launch_act(ptr[(size_t)s.in], ld[(size_t)s.in], ptr[(size_t)s.out], ld[(size_t)s.out],
+                               P.buf_rows[(size_t)s.out], cnt, s.act, stream);
+                launches++;
+                break;
+        }
+        if (e != cudaSuccess)
+            return Status::Err(ROSENNA_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(e));
+    }
+    g_launches += launches;
+    return Status::Ok();
+}
+
+Status check_batch(int64_t n) {
+    if (n < 0) return Status::Err(ROSENNA_ERR_ARG, "negative batch size");
+    for (auto *v : {&g_ctx.plan.inputs, &g_ctx.plan.outputs})
+        for (auto &io : *v)
+            if (io.pre > 1 && n != 1)
+                return Status::Err(ROSENNA_ERR_UNSUPPORTED,
+                                   "an output merges the batch into another dimension; only n == 1 runs");
+    return Status::Ok();
+}
+
+Device *device_by_id(int id) {
+    for (auto &d : g_ctx.devs)
+        if (d->id == id) return d.get();
+    return nullptr;
+}
+
+// Host path on one device: samples [a, b) of arrays with batch n.
+Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const *in, float *const *out) {
+    CUDA_TRY(cudaSetDevice(d.id));
+    const Plan &P = g_ctx.plan;
+    const int64_t total = b - a;
+    if (total <= 0) return Status::Ok();
+    const int64_t chunk = std::min<int64_t>(max_chunk(total), (int64_t)1 << 20);
+    for (int k = 0; k < kSlots; k++) {
+        Status st = ensure_scratch(d.slots[k], std::min(chunk, total));
+        if (!st.ok()) return st;
+        if (!(st = ensure_io(d.slots[k], std::min(chunk, total))).ok()) return st;
+    }
+    int64_t ci = 0;
+    for (int64_t c0 = a; c0 < b; c0 += chunk, ci++) {
+        Slot &s = d.slots[ci % kSlots];
+        const int64_t cnt = std::min(chunk, b - c0);
+        std::vector<float *> ptr(P.buf_rows.size(), nullptr);
+        std::vector<int64_t> ld(P.buf_rows.size(), 0);
+        for (size_t bi = 0; bi < ptr.size(); bi++) {
+            ptr[bi] = s.io.empty() || !s.io[bi] ? s.scratch[bi] : s.io[bi];
+            ld[bi] = s.io.empty() || !s.io[bi] ? s.cap : s.io_cap;
+        }
+        for (size_t i = 0; i < P.inputs.size(); i++) {
+            const IoDesc &io = P.inputs[i];
+            CUDA_TRY(cudaMemcpy2DAsync(s.io[(size_t)io.buf], sizeof(float) * (size_t)s.io_cap, in[i] + c0,
+                                       sizeof(float) * (size_t)n, sizeof(float) * (size_t)cnt, (size_t)io.rows,
+                                       cudaMemcpyHostToDevice, s.stream));
+        }
+        Status st = run_plan(d, ptr, ld, cnt, s.stream);
+        if (!st.ok()) return st;
+        for (size_t i = 0; i < P.outputs.size(); i++) {
+            const IoDesc &io = P.outputs[i];
+            CUDA_TRY(cudaMemcpy2DAsync(out[i] + c0, sizeof(float) * (size_t)n, s.io[(size_t)io.buf],
+                                       sizeof(float) * (size_t)s.io_cap, sizeof(float) * (size_t)cnt, (size_t)io.rows,
+                                       cudaMemcpyDeviceToHost, s.stream));
+        }
+    }
+    for (auto &s : d.slots) CUDA_TRY(cudaStreamSynchronize(s.stream));
+    CUDA_TRY(cudaGetLastError());
+    return Status::Ok();
+}
+
+Status do_initialize(const std::string &model, const std::string &weights, const std::string &vars) {
+    release_all();
+    g_ctx.mf = ModelFiles();
+    Status st = read_model_files(model, weights, vars, &g_ctx.mf);
+    if (!st.ok()) return st;
+    if (!(st = build_plan(g_ctx.mf, &g_ctx.plan)).ok()) return st;
+    Plan &P = g_ctx.plan;
+    // layer tables of the MLP steps go into the arena too
+    g_ctx.mlp_tables.clear();
+    g_ctx.mlp_table_off.assign(P.steps.size(), -1);
+    g_ctx.mlp_table_arena_off.assign(P.steps.size(), -1);
+    for (size_t i = 0; i < P.steps.size(); i++) {
+        const Step &s = P.steps[i];
+        if (s.kind != Step::MLP) continue;
+        if ((int)s.layers.size() > kMaxMlpLayers) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "MLP chain longer than 24 layers");
+        g_ctx.mlp_table_off[i] = (int64_t)g_ctx.mlp_tables.size();
+        std::vector<MlpLayerDev> t;
+        for (auto &l : s.layers) t.push_back(MlpLayerDev{l.K, l.M, l.Kp, l.Mp, l.act, 0, l.w_off, l.b_off});
+        int S = 0;
+        if (!mlp_smem_bytes(t.data(), (int)t.size(), &S))
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED, "an MLP layer is too wide for the fused kernel");
+        g_ctx.mlp_tables.insert(g_ctx.mlp_tables.end(), t.begin(), t.end());
+        size_t off = (P.arena.size() + 3) / 4 * 4;
+        size_t words = t.size() * sizeof(MlpLayerDev) / sizeof(float);
+        P.arena.resize(off + words, 0.f);
+        std::memcpy(P.arena.data() + off, t.data(), t.size() * sizeof(MlpLayerDev));
+        P.arena.resize((P.arena.size() + 3) / 4 * 4, 0.f);
+        g_ctx.mlp_table_arena_off[i] = (int64_t)off;
+    }
+    for (auto &s : P.steps) {
+        int S = 0;
+        if (s.kind == Step::LSTM && !lstm_smem_bytes(s.Ip, s.Hp, &S))
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED, "LSTM hidden size too large for the on-chip kernel");
+    }
+    g_ctx.is_io_in.assign(P.buf_rows.size(), false);
+    g_ctx.is_io_out.assign(P.buf_rows.size(), false);
+    for (auto &io : P.inputs) g_ctx.is_io_in[(size_t)io.buf] = true;
+    for (auto &io : P.outputs) g_ctx.is_io_out[(size_t)io.buf] = true;
+    g_ctx.desc = P.describe();
+
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0)
+        return Status::Err(ROSENNA_ERR_NO_DEVICE, "no CUDA device is visible");
+    std::vector<int> ids = g_ctx.device_ids;
+    if (ids.empty())
+        for (int i = 0; i < count; i++) ids.push_back(i);
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (int id : ids) {
+        if (id < 0 || id >= count) return Status::Err(ROSENNA_ERR_NO_DEVICE, "device id out of range");
+        auto d = std::make_unique<Device>();
+        d->id = id;
+        CUDA_TRY(cudaSetDevice(id));
+        int major = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, id);
+        if (major < 10) return Status::Err(ROSENNA_ERR_NO_DEVICE, "device is not sm_100 (B200)");
+        cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, id);
+        CUDA_TRY(configure_kernels());
+        CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
+        CUDA_TRY(cudaMemcpy(d->arena, P.arena.data(), sizeof(float) * P.arena.size(), cudaMemcpyHostToDevice));
+        for (auto &s : d->slots) {
+            CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+            CUDA_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+        }
+        g_ctx.devs.push_back(std::move(d));
+    }
+    cudaSetDevice(cur);
+    g_ctx.ready = true;
+    return Status::Ok();
+}
+
+int report(const Status &st) { return st.ok() ? ok() : fail(st.code, st.msg); }
+
+}  // namespace
+}  // namespace rosenna
+
+using namespace rosenna;
+
+extern "C" {
+
+int rosenna_initialize_from(const char *model_txt, const char *weights_txt, const char *variables_fpp) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!model_txt || !weights_txt) return fail(ROSENNA_ERR_ARG, "null path");
+    std::string vars;
+    if (variables_fpp) {
+        vars = variables_fpp;
+    } else {
+        std::string m(model_txt);
+        size_t p = m.find_last_of('/');
+        vars = (p == std::string::npos ? std::string() : m.substr(0, p + 1)) + "variables.fpp";
+    }
+    Status st = do_initialize(model_txt, weights_txt, vars);
+    if (!st.ok()) release_all();
+    return report(st);
+}
+
+int rosenna_check_model(const char *model_txt, const char *weights_txt, const char *variables_fpp) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!model_txt || !weights_txt) return fail(ROSENNA_ERR_ARG, "null path");
+    std::string vars;
+    if (variables_fpp) {
+        vars = variables_fpp;
+    } else {
+        std::string m(model_txt);
+        size_t p = m.find_last_of('/');
+        vars = (p == std::string::npos ? std::string() : m.substr(0, p + 1)) + "variables.fpp";
+    }
+    ModelFiles mf;
+    Plan plan;
+    Status st = read_model_files(model_txt, weights_txt, vars, &mf);
+    if (st.ok()) st = build_plan(mf, &plan);
+    if (st.ok()) g_ctx.desc = plan.describe();
+    return report(st);
+}
+
+int rosenna_initialize(void) { return rosenna_initialize_from("onnxModel.txt", "onnxWeights.txt", "variables.fpp"); }
+
+void initialize(void) { (void)rosenna_initialize(); }
+
+int rosenna_finalize(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    release_all();
+    g_ctx.plan = Plan();
+    g_ctx.mf = ModelFiles();
+    return ok();
+}
+
+int rosenna_set_devices(const int *ids, int count) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (count < 0 || (count > 0 && !ids)) return fail(ROSENNA_ERR_ARG, "bad device list");
+    g_ctx.device_ids.assign(ids, ids + count);
+    return ok();
+}
+
+int rosenna_last_status(void) { return g_status; }
+const char *rosenna_last_error(void) { return g_error.c_str(); }
+
+int rosenna_num_inputs(void) { return g_ctx.ready ? (int)g_ctx.plan.inputs.size() : -ROSENNA_ERR_STATE; }
+int rosenna_num_outputs(void) { return g_ctx.ready ? (int)g_ctx.plan.outputs.size() : -ROSENNA_ERR_STATE; }
+
+static int io_shape(const std::vector<IoDesc> &v, int i, int64_t *dims, int max_dims, int *bdim) {
+    if (!g_ctx.ready) return -ROSENNA_ERR_STATE;
+    if (i < 0 || i >= (int)v.size()) return -ROSENNA_ERR_ARG;
+    const IoDesc &d = v[(size_t)i];
+    for (int k = 0; k < (int)d.shape.size() && k < max_dims; k++) dims[k] = d.shape[(size_t)k];
+    if (bdim) *bdim = d.bdim;
+    return (int)d.shape.size();
+}
+
+int rosenna_input_shape(int i, int64_t *dims, int max_dims, int *bdim) { return io_shape(g_ctx.plan.inputs, i, dims, max_dims, bdim); }
+int rosenna_output_shape(int i, int64_t *dims, int max_dims, int *bdim) { return io_shape(g_ctx.plan.outputs, i, dims, max_dims, bdim); }
+
+int rosenna_use_model_f32(int64_t n, const float *const *inputs, float *const *outputs) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    Status st = check_batch(n);
+    if (!st.ok()) return report(st);
+    if (!inputs || !outputs) return fail(ROSENNA_ERR_ARG, "null input/output array list");
+    for (size_t i = 0; i < g_ctx.plan.inputs.size(); i++)
+        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
+    for (size_t i = 0; i < g_ctx.plan.outputs.size(); i++)
+        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
+    g_launches = 0;
+    if (n == 0) return ok();
+    int cur = 0;
+    cudaGetDevice(&cur);
+    const int G = (int)g_ctx.devs.size();
+    std::vector<Status> res((size_t)G);
+    std::vector<std::thread> th;
+    for (int g = 0; g < G; g++) {
+        // contiguous split; the first n % G ranks take one extra sample
+        const int64_t base = n / G, rem = n % G;
+        const int64_t a = g * base + std::min<int64_t>(g, rem), b = a + base + (g < rem ? 1 : 0);
+        th.emplace_back([&, g, a, b] { res[(size_t)g] = host_range(*g_ctx.devs[(size_t)g], n, a, b, inputs, outputs); });
+    }
+    for (auto &t : th) t.join();
+    cudaSetDevice(cur);
+    for (auto &r : res)
+        if (!r.ok()) return report(r);
+    return ok();
+}
+
+int rosenna_use_model_f64(int64_t n, const double *const *inputs, double *const *outputs) {
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    if (n < 0 || !inputs || !outputs) return fail(ROSENNA_ERR_ARG, "bad arguments");
+    const Plan &P = g_ctx.plan;
+    std::vector<std::vector<float>> fi(P.inputs.size()), fo(P.outputs.size());
+    std::vector<const float *> pi;
+    std::vector<float *> po;
+    for (size_t i = 0; i < P.inputs.size(); i++) {
+        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
+        size_t cnt = (size_t)(P.inputs[i].rows * n);
+        fi[i].resize(cnt);
+        for (size_t k = 0; k < cnt; k++) fi[i][k] = (float)inputs[i][k];
+        pi.push_back(fi[i].data());
+    }
+    for (size_t i = 0; i < P.outputs.size(); i++) {
+        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
+        fo[i].resize((size_t)(P.outputs[i].rows * n));
+        po.push_back(fo[i].data());
+    }
+    int rc = rosenna_use_model_f32(n, pi.data(), po.data());
+    if (rc) return rc;
+    for (size_t i = 0; i < P.outputs.size(); i++)
+        for (size_t k = 0; k < fo[i].size(); k++) outputs[i][k] = fo[i][k];
+    return ok();
+}
+
+int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *const *outputs, void *stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    Status st = check_batch(n);
+    if (!st.ok()) return report(st);
+    if (!inputs || !outputs) return fail(ROSENNA_ERR_ARG, "null input/output array list");
+    g_launches = 0;
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaGetDevice failed");
+    // with one selected GPU that GPU is used; otherwise the current device
+    Device *d = g_ctx.devs.size() == 1 ? g_ctx.devs[0].get() : device_by_id(cur);
+    if (!d) return fail(ROSENNA_ERR_NO_DEVICE, "the current device was not initialized");
+    if (n == 0) return ok();
+    struct Restore {
+        int dev;
+        ~Restore() { cudaSetDevice(dev); }
+    } restore{cur};
+    if (cudaSetDevice(d->id) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaSetDevice failed");
+    const Plan &P = g_ctx.plan;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t chunk = max_chunk(n);
+    st = ensure_scratch(d->slots[0], chunk);
+    if (!st.ok()) return report(st);
+    // the scratch buffers are shared by every device-path call on this device
+    if (cudaStreamWaitEvent(s, d->slots[0].done, 0) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaStreamWaitEvent failed");
+    for (int64_t c0 = 0; c0 < n; c0 += chunk) {
+        const int64_t cnt = std::min(chunk, n - c0);
+        std::vector<float *> ptr(P.buf_rows.size(), nullptr);
+        std::vector<int64_t> ld(P.buf_rows.size(), d->slots[0].cap);
+        for (size_t b = 0; b < ptr.size(); b++) ptr[b] = d->slots[0].scratch.empty() ? nullptr : d->slots[0].scratch[b];
+        for (size_t i = 0; i < P.inputs.size(); i++) {
+            if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
+            ptr[(size_t)P.inputs[i].buf] = const_cast<float *>(inputs[i]) + c0;
+            ld[(size_t)P.inputs[i].buf] = n;
+        }
+        for (size_t i = 0; i < P.outputs.size(); i++) {
+            if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
+            ptr[(size_t)P.outputs[i].buf] = outputs[i] + c0;
+            ld[(size_t)P.outputs[i].buf] = n;
+        }
+        st = run_plan(*d, ptr, ld, cnt, s);
+        if (!st.ok()) return report(st);
+    }
+    if (cudaEventRecord(d->slots[0].done, s) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaEventRecord failed");
+    return ok();
+}
+
+int64_t rosenna_last_launch_count(void) { return g_launches.load(); }
+
+const char *rosenna_plan_description(void) { return g_ctx.desc.c_str(); }
+
+}  // extern "C"

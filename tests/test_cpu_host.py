@@ -1,0 +1,113 @@
+"""Host-side tests that need no GPU: the C-ABI library, the plan builder, the
+model-file reader/writer, error statuses, and the oracle on the workloads."""
+import os
+import re
+import shutil
+
+import numpy as np
+import pytest
+
+from oracle.oracle import OracleModel
+from rosenna_b200 import api, workloads
+from tests import goldens
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_exports_every_declared_symbol():
+    with open(os.path.join(ROOT, "include", "rosenna.h")) as f:
+        header = f.read()
+    declared = set(re.findall(r"^\s*(?:void|int|int64_t|const char \*)\s*\*?(\w+)\(", header, re.M))
+    assert declared == set(api.EXPORTS)
+    L = api.lib()
+    for name in declared:
+        assert hasattr(L, name), name
+
+
+@pytest.mark.parametrize("case", goldens.cases())
+def test_plan_builds_for_golden_case(case):
+    desc = api.check_model(goldens.case_dir(case))
+    assert desc.strip()
+
+
+def test_plan_fuses_the_workloads(tmp_path):
+    expect = {
+        "small_mlp": ["mlp b0->b1 [10x64:tanh 64x64:tanh 64x64:tanh 64x5]"],
+        "wide_mlp": ["mlp b0->b1 [16x256:relu 256x256:relu 256x256:relu 256x256:relu 256x256:relu 256x8]"],
+        "lstm": ["lstm b0 T=50 I=8 H=32", "mlp"],
+        "cnn": ["conv", "relu maxpool k=2 s=2 -> 14x14", "relu avgpool k=2 s=2 -> 7x7", "mlp"],
+        "lstm2": ["lstm b0 T=100 I=12 H=64", "lstm b5 T=100 I=64 H=64", "mlp"],
+    }
+    for name, parts in expect.items():
+        d = tmp_path / name
+        workloads.write_model(name, str(d))
+        desc = api.check_model(str(d))
+        for p in parts:
+            assert p in desc, (name, desc)
+
+
+def test_initialize_statuses(tmp_path):
+    # missing files: I/O error; no GPU here: no-device error; state error before init
+    with pytest.raises(api.RosennaError) as e:
+        api.initialize(str(tmp_path / "nope"))
+    assert e.value.code == api.ERR_IO
+    with pytest.raises(api.RosennaError) as e:
+        api.use_model([np.zeros((1, 2), np.float32)])
+    assert e.value.code == api.ERR_STATE
+
+
+def test_initialize_without_gpu_reports_no_device():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(api.RosennaError) as e:
+        api.initialize(goldens.case_dir("gemm_small"))
+    assert e.value.code == api.ERR_NO_DEVICE
+
+
+def test_malformed_and_unsupported_models(tmp_path):
+    src = goldens.case_dir("gemm_small")
+    d = tmp_path / "m"
+    shutil.copytree(src, d)
+    # truncated weights file
+    with open(d / "onnxWeights.txt", "w") as f:
+        f.write("0.5 0.25\n")
+    with pytest.raises(api.RosennaError) as e:
+        api.check_model(str(d))
+    assert e.value.code == api.ERR_FORMAT
+    # an op the engine does not run
+    shutil.copytree(src, tmp_path / "u")
+    v = (tmp_path / "u" / "variables.fpp").read_text().replace("('Relu', ['input'], [2])", "('Add', ['input'], [2])", 1)
+    (tmp_path / "u" / "variables.fpp").write_text(v)
+    with pytest.raises(api.RosennaError) as e:
+        api.check_model(str(tmp_path / "u"))
+    assert e.value.code == api.ERR_UNSUPPORTED
+    # a broken variables.fpp literal
+    shutil.copytree(src, tmp_path / "b")
+    (tmp_path / "b" / "variables.fpp").write_text("#:set architecture = [('Gemm', ['input', 1], None\n")
+    with pytest.raises(api.RosennaError) as e:
+        api.check_model(str(tmp_path / "b"))
+    assert e.value.code == api.ERR_FORMAT
+
+
+@pytest.mark.parametrize("name", list(workloads.WORKLOADS))
+def test_oracle_matches_torch_on_workloads(name, tmp_path):
+    mod = workloads.write_model(name, str(tmp_path))
+    n = 5
+    ins = workloads.make_inputs(name, n)
+    out = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+    ref = workloads.torch_reference(name, mod, ins)[0]
+    np.testing.assert_allclose(out.reshape(ref.shape), ref, rtol=0, atol=1e-12)
+
+
+def test_writer_weights_round_trip(tmp_path):
+    """Values printed by the writer read back to the exact fp32 weights (modelParserONNX.py:82-86)."""
+    import torch
+
+    mod = workloads.write_model("small_mlp", str(tmp_path))
+    lines = (tmp_path / "onnxWeights.txt").read_text().splitlines()
+    w0 = np.array([float(v) for v in lines[0].split()])
+    ref = mod[0].weight.detach().numpy().astype(np.float64).flatten(order="F")
+    assert np.array_equal(w0, ref)
+    assert torch.float32 == mod[0].weight.dtype

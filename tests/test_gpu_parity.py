@@ -1,0 +1,130 @@
+"""Parity of the CUDA engine (through the C ABI) with the fp64 oracle and the
+golden fixtures.  Tolerance, per element: |gpu - ref| <= 1e-5 + 1e-4 * |ref|
+(fp32 engine against fp64 reference; the reference's own checker uses an
+absolute 1e-5, test/testChecker.py:14-17)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle.oracle import OracleModel
+from rosenna_b200 import api, workloads
+from tests import goldens
+
+pytestmark = pytest.mark.gpu
+
+ABS, REL = 1e-5, 1e-4
+
+
+def assert_close(out, ref, what=""):
+    out = np.asarray(out, dtype=np.float64).reshape(np.shape(ref))
+    err = np.abs(out - ref)
+    bad = err > ABS + REL * np.abs(ref)
+    rel = err / np.maximum(np.abs(ref), 1e-30)
+    assert not bad.any(), f"{what}: {bad.sum()} elements out of tolerance; max abs {err.max():.3e}, max rel {rel.max():.3e}"
+
+
+@pytest.fixture(autouse=True)
+def _device():
+    assert torch.cuda.is_available(), "gpu tests need a CUDA device"
+    api.set_devices([0])
+    yield
+    api.finalize()
+
+
+@pytest.mark.parametrize("case", goldens.cases())
+def test_golden_case_at_export_batch(case):
+    """Each reference case at its export shapes against PyTorch's fp64 output."""
+    api.initialize(goldens.case_dir(case))
+    ins = goldens.inputs(case)
+    specs = api.input_specs()
+    n = ins[0].shape[specs[0][1]]
+    out = api.use_model(ins, n=n)[0]
+    assert api.last_launch_count() > 0
+    assert_close(out, goldens.golden(case), case)
+
+
+BATCHED_CASES = [c for c in goldens.cases() if c not in ("conv_basic", "lstm_gemm")]
+
+
+@pytest.mark.parametrize("case", BATCHED_CASES)
+@pytest.mark.parametrize("n", [1, 3, 129, 1000])
+def test_golden_case_batched(case, n):
+    """The reference case widened to a batch of n random samples, against the
+    oracle calling use_model once per sample."""
+    d = goldens.case_dir(case)
+    api.initialize(d)
+    rng = np.random.default_rng(n)
+    rows = [int(np.prod(s)) // s[b] for s, b in api.input_specs()]
+    ins = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) for r in rows]
+    out = api.use_model_rows(ins)[0]
+    ref = OracleModel(d).run_batched(n, ins, [1] * len(ins), [1])[0]
+    assert_close(out, ref.reshape(out.shape), f"{case} n={n}")
+
+
+def test_merged_batch_output_runs_only_at_batch_one():
+    """lstm_gemm reshapes (N,T,H) to (N*T,H): its output mixes samples, so only n=1 runs."""
+    api.initialize(goldens.case_dir("lstm_gemm"))
+    ins = [np.ones((3, 2, 5), np.float32), np.ones((1, 3, 2), np.float32), np.ones((1, 3, 2), np.float32)]
+    with pytest.raises(api.RosennaError) as e:
+        api.use_model(ins, n=3)
+    assert e.value.code == api.ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("name", list(workloads.WORKLOADS))
+@pytest.mark.parametrize("n", [1, 7, 1000, 4099])
+def test_workload_parity(name, n, tmp_path):
+    workloads.write_model(name, str(tmp_path))
+    api.initialize(str(tmp_path))
+    ins = workloads.make_inputs(name, n, seed_offset=n)
+    out = api.use_model_rows(ins)[0]
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+    assert_close(out, ref.reshape(out.shape), f"{name} n={n}")
+
+
+@pytest.mark.parametrize("name", ["small_mlp", "wide_mlp", "lstm", "cnn"])
+def test_device_path_matches_host_path(name, tmp_path):
+    workloads.write_model(name, str(tmp_path))
+    api.initialize(str(tmp_path))
+    n = 5003
+    ins = workloads.make_inputs(name, n, seed_offset=11)
+    host = api.use_model_rows(ins)[0]
+    dins = [torch.from_numpy(x).cuda() for x in ins]
+    dout = torch.zeros(host.shape, dtype=torch.float32, device="cuda")
+    api.use_model_device(n, [x.data_ptr() for x in dins], [dout.data_ptr()], torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(dout.cpu().numpy(), host)
+
+
+def test_large_batch_small_mlp_chunks_and_tails(tmp_path):
+    """More samples than one host chunk (2^20), with an odd tail."""
+    workloads.write_model("small_mlp", str(tmp_path))
+    api.initialize(str(tmp_path))
+    n = (1 << 20) + 333
+    ins = workloads.make_inputs("small_mlp", n, seed_offset=3)
+    out = api.use_model_rows(ins)[0]
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
+    assert_close(out, ref.reshape(out.shape), "small_mlp large")
+
+
+def test_fp64_entry_point(tmp_path):
+    workloads.write_model("small_mlp", str(tmp_path))
+    api.initialize(str(tmp_path))
+    ins = workloads.make_inputs("small_mlp", 100)
+    o32 = api.use_model_rows(ins)[0]
+    x64 = np.asfortranarray(ins[0].astype(np.float64).T)  # logical (n, 10), Fortran order
+    o64 = api.use_model([x64], n=100, dtype=np.float64)[0]
+    assert np.array_equal(o64.T.astype(np.float32), o32)
+
+
+def test_multi_gpu_split_matches(tmp_path):
+    count = torch.cuda.device_count()
+    if count < 2:
+        pytest.skip("one GPU visible")
+    api.set_devices(list(range(min(count, 4))))
+    workloads.write_model("lstm", str(tmp_path))
+    api.initialize(str(tmp_path))
+    n = 10007
+    ins = workloads.make_inputs("lstm", n, seed_offset=5)
+    out = api.use_model_rows(ins)[0]
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
+    assert_close(out, ref.reshape(out.shape), "lstm multi-gpu")
