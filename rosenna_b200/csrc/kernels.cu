@@ -27,7 +27,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kKC = 32;  // weight rows per streamed chunk
-constexpr size_t kMaxSmem = 227 * 1024;
+constexpr size_t kMaxSmem = 226 * 1024;  // dynamic budget; leaves room for static shared memory
 
 // ---- activations -----------------------------------------------------------
 // tanh(x) = 1 - 2 / (1 + e^{2x}) and sigmoid(x) = 1 / (1 + e^{-x}), with
