@@ -94,6 +94,21 @@ int rosenna_use_model_f64(int64_t n, const double *const *inputs, double *const 
  * stream reaches this work. */
 int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *const *outputs, void *stream);
 
+/* Allocation-free variant of rosenna_use_model_device_f32.  It has no
+ * counterpart in roseNNa.  For callers that cannot let the library allocate
+ * device memory during the call: a solver whose own pool allocator holds all
+ * free GPU memory, or a time-step loop that cannot absorb the device-wide
+ * synchronisation of cudaMalloc/cudaFree.  The plan's intermediate buffers come
+ * from one fixed 64 MiB array in device memory that every GPU loading this
+ * library holds until exit; n is rejected (ROSENNA_ERR_SHAPE, with the limit in
+ * rosenna_last_error()) when the intermediates for n samples do not fit.  The
+ * first call on a device looks up that array's address (set-up); make that
+ * first call before any stream capture.  All calls share the array and it keeps
+ * the last call's contents (no intermediate needs clearing: each is written
+ * before it is read), so calls whose work overlaps on the GPU race: order them
+ * on one stream.  Arguments and layout as for rosenna_use_model_device_f32. */
+int rosenna_use_model_device_noalloc_f32(int64_t n, const float *const *inputs, float *const *outputs, void *stream);
+
 /* Number of kernel launches the last use_model call issued (all devices). */
 int64_t rosenna_last_launch_count(void);
 

@@ -27,7 +27,8 @@ EXPORTS = [
     "initialize", "rosenna_initialize", "rosenna_initialize_from", "rosenna_check_model", "rosenna_finalize",
     "rosenna_set_devices", "rosenna_last_status", "rosenna_last_error", "rosenna_num_inputs", "rosenna_num_outputs",
     "rosenna_input_shape", "rosenna_output_shape", "rosenna_use_model_f32", "rosenna_use_model_f64",
-    "rosenna_use_model_device_f32", "rosenna_last_launch_count", "rosenna_plan_description",
+    "rosenna_use_model_device_f32", "rosenna_use_model_device_noalloc_f32", "rosenna_last_launch_count",
+    "rosenna_plan_description",
 ]
 
 
@@ -66,6 +67,7 @@ def lib():
     L.rosenna_use_model_f32.argtypes = [c_i64, PP, PP]
     L.rosenna_use_model_f64.argtypes = [c_i64, PP, PP]
     L.rosenna_use_model_device_f32.argtypes = [c_i64, PP, PP, c_void_p]
+    L.rosenna_use_model_device_noalloc_f32.argtypes = [c_i64, PP, PP, c_void_p]
     L.rosenna_last_launch_count.restype = c_i64
     L.rosenna_plan_description.restype = c_char_p
     _lib = L
@@ -197,3 +199,9 @@ def use_model_rows(inputs_rows: Sequence[np.ndarray], n: Optional[int] = None) -
         outs.append(np.zeros((rows, n), dtype=np.float32))
     _check(lib().rosenna_use_model_f32(n, _ptrs([a.ctypes.data for a in ins]), _ptrs([a.ctypes.data for a in outs])))
     return outs
+
+
+def use_model_device_noalloc(n: int, in_ptrs: Sequence[int], out_ptrs: Sequence[int], stream: int = 0) -> None:
+    """The allocation-free device entry point (no cudaMalloc/cudaFree during the
+    call; intermediates come from a fixed 64 MiB array per GPU, so n is bounded)."""
+    _check(lib().rosenna_use_model_device_noalloc_f32(n, _ptrs(in_ptrs), _ptrs(out_ptrs), ctypes.c_void_p(stream)))

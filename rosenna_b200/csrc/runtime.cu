@@ -571,3 +571,96 @@ int64_t rosenna_last_launch_count(void) { return g_launches.load(); }
 const char *rosenna_plan_description(void) { return g_ctx.desc.c_str(); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free use_model on device arrays.
+//
+// Some callers cannot have the library allocate device memory while they run:
+// a solver that hands all free GPU memory to its own pool allocator at start-up
+// (cudaMalloc would then fail), or a time-step loop that must not stall, since
+// cudaMalloc/cudaFree synchronise the device.  rosenna_use_model_device_f32
+// allocates its intermediate buffers on first use; this entry point instead
+// carves them from one fixed array in device memory that every GPU loading
+// this library holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace rosenna {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)64 << 20;  // 64 MiB per GPU
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// device address of g_noalloc_scratch per device id, looked up once per device
+std::vector<void *> g_noalloc_addr;
+
+}  // namespace
+}  // namespace rosenna
+
+extern "C" int rosenna_use_model_device_noalloc_f32(int64_t n, const float *const *inputs, float *const *outputs,
+                                                    void *stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    Status st = check_batch(n);
+    if (!st.ok()) return report(st);
+    if (!inputs || !outputs) return fail(ROSENNA_ERR_ARG, "null input/output array list");
+    const Plan &P = g_ctx.plan;
+    for (size_t i = 0; i < P.inputs.size(); i++)
+        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
+    for (size_t i = 0; i < P.outputs.size(); i++)
+        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
+    g_launches = 0;
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaGetDevice failed");
+    Device *d = g_ctx.devs.size() == 1 ? g_ctx.devs[0].get() : device_by_id(cur);
+    if (!d) return fail(ROSENNA_ERR_NO_DEVICE, "the current device was not initialized");
+    if (n == 0) return ok();
+
+    // intermediates of the plan, each rows x n floats, 256-byte aligned
+    std::vector<bool> used(P.buf_rows.size(), false);
+    for (auto &s : P.steps)
+        for (int b : {s.in, s.out, s.h0, s.c0, s.y, s.hn, s.cn})
+            if (b >= 0) used[(size_t)b] = true;
+    std::vector<size_t> off(P.buf_rows.size(), 0);
+    size_t need = 0;
+    for (size_t b = 0; b < used.size(); b++) {
+        if (!used[b] || !is_scratch((int)b)) continue;
+        off[b] = need;
+        need += ((size_t)P.buf_rows[b] * (size_t)n * sizeof(float) + 255) / 256 * 256;
+    }
+    if (need > kNoAllocScratchBytes) {
+        size_t per_sample = 0;
+        for (size_t b = 0; b < used.size(); b++)
+            if (used[b] && is_scratch((int)b)) per_sample += (size_t)P.buf_rows[b] * sizeof(float);
+        char msg[256];
+        snprintf(msg, sizeof msg,
+                 "n=%lld needs %zu bytes of intermediates; the allocation-free entry point has %zu bytes "
+                 "(at most about %zu samples for this model)",
+                 (long long)n, need, kNoAllocScratchBytes, per_sample ? kNoAllocScratchBytes / per_sample : 0);
+        return fail(ROSENNA_ERR_SHAPE, msg);
+    }
+
+    struct Restore {
+        int dev;
+        ~Restore() { cudaSetDevice(dev); }
+    } restore{cur};
+    if (cudaSetDevice(d->id) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaSetDevice failed");
+    // set-up, once per device, with that device current
+    if ((int)g_noalloc_addr.size() <= d->id) g_noalloc_addr.resize((size_t)d->id + 1, nullptr);
+    if (!g_noalloc_addr[(size_t)d->id]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(ROSENNA_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+        g_noalloc_addr[(size_t)d->id] = p;
+    }
+    unsigned char *base = static_cast<unsigned char *>(g_noalloc_addr[(size_t)d->id]);
+
+    std::vector<float *> ptr(P.buf_rows.size(), nullptr);
+    std::vector<int64_t> ld(P.buf_rows.size(), n);
+    for (size_t b = 0; b < used.size(); b++)
+        if (used[b] && is_scratch((int)b)) ptr[b] = reinterpret_cast<float *>(base + off[b]);
+    for (size_t i = 0; i < P.inputs.size(); i++) ptr[(size_t)P.inputs[i].buf] = const_cast<float *>(inputs[i]);
+    for (size_t i = 0; i < P.outputs.size(); i++) ptr[(size_t)P.outputs[i].buf] = outputs[i];
+    st = run_plan(*d, ptr, ld, n, reinterpret_cast<cudaStream_t>(stream));
+    return report(st);
+}
