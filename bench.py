@@ -127,6 +127,14 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
 def measured_fp32_peak(torch):
     """cuBLAS SGEMM (TF32 off), 8192^3, best of 5: the FP32 FFMA denominator."""
     prev = torch.backends.cuda.matmul.allow_tf32
@@ -248,15 +256,27 @@ def main():
     ok_out = bool(torch.isfinite(h_out[0]).all())
 
     # ---- roofline of the dominant kernel ----
-    fp32_peak = measured_fp32_peak(torch) if rank == 0 else None
     kernel_s = t_dev / max(1, args.steps * launches_per_step) if launches_per_step == 1 else None
     achieved = (w.flops_per_sample * n) / kernel_s / 1e12 if kernel_s else None
-    roof = {"bound": "fp32", "kernel": "mlp_ffma_kernel" if "mlp" in args.workload else "plan",
-            "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-            "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
-            "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (MEASURED_PEAKS.json has no FP32 figure)",
-            "traffic": NCU_TRAFFIC.get(args.workload),
-            "algorithmic_flops_per_launch": w.flops_per_sample * n if kernel_s else None}
+    if "mlp_tc" in plan:
+        # 3xTF32: three TF32 tensor products per fp32 MAC; TF32 runs at half the bf16 rate
+        peaks = measured_peaks()
+        bf16 = peaks.get("bf16_tflops")
+        src = "MEASURED_PEAKS.json" if bf16 else "fallback 1590 TFLOP/s bf16 burst"
+        bf16 = bf16 or 1590.0
+        peak = bf16 / 2.0 / 3.0
+        roof = {"bound": "tensor", "kernel": "mlp_tc_kernel", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
+                "peak_source": f"{src}: bf16 {bf16:.0f} TFLOP/s burst / 2 (TF32 rate) / 3 (3xTF32), of measured",
+                "tensor_pipe_frac": (achieved * 6.0 / bf16) if achieved else None}
+    else:
+        fp32_peak = measured_fp32_peak(torch) if rank == 0 else None
+        roof = {"bound": "fp32", "kernel": "mlp_ffma_kernel" if "mlp" in args.workload else "plan",
+                "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+                "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
+                "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (MEASURED_PEAKS.json has no FP32 figure)"}
+    roof["traffic"] = NCU_TRAFFIC.get((args.workload, roof["kernel"]))
+    roof["algorithmic_flops_per_launch"] = w.flops_per_sample * n if kernel_s else None
 
     if rank == 0:
         cb = None

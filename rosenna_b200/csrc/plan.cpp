@@ -128,6 +128,17 @@ bool per_sample_map(const Shape &S, int b, const Shape &R, int b2, const std::ve
     return true;
 }
 
+// fp32 -> tf32 (10 mantissa bits), round to nearest with ties away from zero,
+// as the device's cvt.rna.tf32.f32 does.
+float tf32_round(float x) {
+    uint32_t b;
+    std::memcpy(&b, &x, 4);
+    if ((b & 0x7f800000u) != 0x7f800000u) b = (b + 0x1000u) & 0xffffe000u;
+    float y;
+    std::memcpy(&y, &b, 4);
+    return y;
+}
+
 bool is_identity(const std::vector<int32_t> &m, int64_t src_rows) {
     if ((int64_t)m.size() != src_rows) return false;
     for (size_t i = 0; i < m.size(); i++)
@@ -262,6 +273,21 @@ Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90
     for (int m = 0; m < M; m++) b[(size_t)m] = (float)L.b.v[(size_t)m];
     ly.w_off = put(wt.data(), wt.size());
     ly.b_off = put(b.data(), b.size());
+    if (M <= 256) {  // tensor-core block: rows n < Np hold tf32(W[n][k]), rows Np + n the rounded remainder
+        ly.tc_Kp = (int)round_up(K, 32);
+        ly.tc_Np = (int)round_up(M, 16);
+        std::vector<float> blk((size_t)2 * ly.tc_Np * ly.tc_Kp, 0.f), tb((size_t)ly.tc_Np, 0.f);
+        for (int n = 0; n < M; n++)
+            for (int k = 0; k < K; k++) {
+                const float w = (float)L.w.v[(size_t)n + (size_t)M * k];
+                const float hi = tf32_round(w);
+                blk[(size_t)n * ly.tc_Kp + k] = hi;
+                blk[(size_t)(ly.tc_Np + n) * ly.tc_Kp + k] = tf32_round(w - hi);
+            }
+        for (int n = 0; n < M; n++) tb[(size_t)n] = (float)L.b.v[(size_t)n];
+        ly.tc_w_off = put(blk.data(), blk.size());
+        ly.tc_b_off = put(tb.data(), tb.size());
+    }
     Step *prev = last_producing(x.buf);
     int out;
     if (prev && prev->kind == Step::MLP && prev->rsub == rsub) {
@@ -679,7 +705,7 @@ std::string Plan::describe() const {
     for (auto &s : steps) {
         switch (s.kind) {
             case Step::MLP:
-                o << "mlp b" << s.in << "->b" << s.out << " [";
+                o << (s.tc ? "mlp_tc b" : "mlp b") << s.in << "->b" << s.out << " [";
                 for (size_t i = 0; i < s.layers.size(); i++)
                     o << (i ? " " : "") << s.layers[i].K << "x" << s.layers[i].M << (s.layers[i].act ? ":" : "")
                       << acts[s.layers[i].act];

@@ -19,10 +19,14 @@ namespace rosenna {
 
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_TANH = 2, ACT_SIGMOID = 3 };
 
-// One Gemm (+ activation) of a fused chain; weights packed as Wt[Kp][Mp] (zero padded).
+// One Gemm (+ activation) of a fused chain; weights packed as Wt[Kp][Mp] (zero
+// padded) for the FFMA kernel and, when M <= 256, as a [2*tc_Np][tc_Kp] block of
+// tf32-rounded high parts and remainders for the tensor-core kernel.
 struct MlpLayer {
     int K = 0, M = 0, Kp = 0, Mp = 0, act = ACT_NONE;
     int64_t w_off = 0, b_off = 0;
+    int tc_Kp = 0, tc_Np = 0;
+    int64_t tc_w_off = -1, tc_b_off = -1;
 };
 
 struct Step {
@@ -33,6 +37,7 @@ struct Step {
     // sub-row t is buffer row t + rsub*k)
     std::vector<MlpLayer> layers;
     int rsub = 1;
+    bool tc = false;  // run on the tensor-core kernel (decided at initialize)
 
     // LSTM: one layer, PyTorch gate order, gate columns interleaved per unit
     int T = 0, I = 0, H = 0, Ip = 0, Hp = 0;

@@ -22,6 +22,7 @@
 
 #include "../../include/rosenna.h"
 #include "kernels.cuh"
+#include "mlp_tc.cuh"
 #include "model_files.hpp"
 #include "plan.hpp"
 
@@ -43,6 +44,9 @@ struct Device {
     int id = 0;
     int num_sms = 148;
     float *arena = nullptr;
+    int *err = nullptr;       // tensor-core kernel status word (0 = ok)
+    int *err_host = nullptr;  // pinned copy, refreshed after each tensor-core launch
+    std::vector<TcArgs> tc_args;  // per plan step (tensor-core MLP steps only)
     Slot slots[kSlots];
 };
 
@@ -103,7 +107,11 @@ void release_device(Device &d) {
         s.done = nullptr;
     }
     cudaFree(d.arena);
+    cudaFree(d.err);
+    if (d.err_host) cudaFreeHost(d.err_host);
     d.arena = nullptr;
+    d.err = nullptr;
+    d.err_host = nullptr;
 }
 
 void release_all() {
@@ -169,6 +177,21 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
         cudaError_t e = cudaSuccess;
         switch (s.kind) {
             case Step::MLP: {
+                if (s.tc) {
+                    TcArgs a = d.tc_args[si];
+                    for (int t = 0; t < s.rsub && e == cudaSuccess; t++) {
+                        a.in = ptr[(size_t)s.in] + (int64_t)t * ld[(size_t)s.in];
+                        a.ld_in = (int64_t)s.rsub * ld[(size_t)s.in];
+                        a.out = ptr[(size_t)s.out] + (int64_t)t * ld[(size_t)s.out];
+                        a.ld_out = (int64_t)s.rsub * ld[(size_t)s.out];
+                        a.n = cnt;
+                        e = launch_mlp_tc(a, d.num_sms, stream);
+                        launches++;
+                    }
+                    if (e == cudaSuccess)
+                        e = cudaMemcpyAsync(d.err_host, d.err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    break;
+                }
                 MlpArgs a{};
                 a.arena = arena;
                 a.layers = reinterpret_cast<const MlpLayerDev *>(arena + g_ctx.mlp_table_arena_off[si]);
@@ -253,8 +276,20 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
     return Status::Ok();
 }
 
+// A tensor-core kernel that timed out leaves a code in its status word; the
+// engine then refuses further calls until it is initialized again.
+Status check_device_status() {
+    for (auto &d : g_ctx.devs)
+        if (d->err_host && *(volatile int *)d->err_host)
+            return Status::Err(ROSENNA_ERR_CUDA, "a tensor-core kernel timed out waiting on its pipeline (code " +
+                                                     std::to_string(*d->err_host) + "); re-run initialize()");
+    return Status::Ok();
+}
+
 Status check_batch(int64_t n) {
     if (n < 0) return Status::Err(ROSENNA_ERR_ARG, "negative batch size");
+    Status st = check_device_status();
+    if (!st.ok()) return st;
     for (auto *v : {&g_ctx.plan.inputs, &g_ctx.plan.outputs})
         for (auto &io : *v)
             if (io.pre > 1 && n != 1)
@@ -308,6 +343,8 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
     }
     for (auto &s : d.slots) CUDA_TRY(cudaStreamSynchronize(s.stream));
     CUDA_TRY(cudaGetLastError());
+    if (d.err_host && *(volatile int *)d.err_host)
+        return Status::Err(ROSENNA_ERR_CUDA, "a tensor-core kernel timed out waiting on its pipeline");
     return Status::Ok();
 }
 
@@ -345,6 +382,20 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         if (s.kind == Step::LSTM && !lstm_smem_bytes(s.Ip, s.Hp, &S))
             return Status::Err(ROSENNA_ERR_UNSUPPORTED, "LSTM hidden size too large for the on-chip kernel");
     }
+    // tensor-core path for MLP chains with a layer >= 128 wide and all <= 256
+    // (ROSENNA_MLP_PATH=ffma forces the FFMA kernel, =tc any eligible chain)
+    const char *path = getenv("ROSENNA_MLP_PATH");
+    const std::string mlp_path = path ? path : "";
+    for (auto &s : P.steps) {
+        if (s.kind != Step::MLP) continue;
+        bool eligible = (int)s.layers.size() <= kTcMaxLayers;
+        int widest = 0;
+        for (auto &l : s.layers) {
+            eligible = eligible && l.tc_w_off >= 0;
+            widest = std::max(widest, l.M);
+        }
+        s.tc = eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 128);
+    }
     g_ctx.is_io_in.assign(P.buf_rows.size(), false);
     g_ctx.is_io_out.assign(P.buf_rows.size(), false);
     for (auto &io : P.inputs) g_ctx.is_io_in[(size_t)io.buf] = true;
@@ -369,8 +420,29 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         if (major < 10) return Status::Err(ROSENNA_ERR_NO_DEVICE, "device is not sm_100 (B200)");
         cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, id);
         CUDA_TRY(configure_kernels());
+        CUDA_TRY(mlp_tc_configure());
         CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
         CUDA_TRY(cudaMemcpy(d->arena, P.arena.data(), sizeof(float) * P.arena.size(), cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMalloc(&d->err, sizeof(int)));
+        CUDA_TRY(cudaMemset(d->err, 0, sizeof(int)));
+        CUDA_TRY(cudaMallocHost(&d->err_host, sizeof(int)));
+        *d->err_host = 0;
+        d->tc_args.assign(P.steps.size(), TcArgs{});
+        for (size_t si = 0; si < P.steps.size(); si++) {
+            const Step &s = P.steps[si];
+            if (!s.tc) continue;
+            TcArgs &a = d->tc_args[si];
+            a.arena = d->arena;
+            a.err = d->err;
+            a.nlayers = (int)s.layers.size();
+            for (int l = 0; l < a.nlayers; l++) {
+                const MlpLayer &ly = s.layers[(size_t)l];
+                a.L[l] = TcLayer{ly.K, ly.M, ly.tc_Kp, ly.tc_Np, ly.tc_Kp / 32, ly.act, ly.tc_w_off, ly.tc_b_off};
+                const char *why = "";
+                if (!mlp_tc_encode_map(&a.maps[l], d->arena + ly.tc_w_off, ly.tc_Kp, ly.tc_Np, &why))
+                    return Status::Err(ROSENNA_ERR_CUDA, why);
+            }
+        }
         for (auto &s : d->slots) {
             CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
             CUDA_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));

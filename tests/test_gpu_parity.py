@@ -128,3 +128,37 @@ def test_multi_gpu_split_matches(tmp_path):
     out = api.use_model_rows(ins)[0]
     ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
     assert_close(out, ref.reshape(out.shape), "lstm multi-gpu")
+
+
+@pytest.mark.parametrize("path", ["tc", "ffma"])
+@pytest.mark.parametrize("name", ["small_mlp", "wide_mlp", "cnn"])
+def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
+    """Both MLP kernels (tcgen05 3xTF32 and FFMA) on every MLP chain shape."""
+    monkeypatch.setenv("ROSENNA_MLP_PATH", path)
+    workloads.write_model(name, str(tmp_path))
+    api.initialize(str(tmp_path))
+    desc = api.plan_description()
+    assert ("mlp_tc" in desc) == (path == "tc"), desc
+    for n in (129, 4099):
+        ins = workloads.make_inputs(name, n, seed_offset=7 + n)
+        out = api.use_model_rows(ins)[0]
+        ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+        assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
+
+
+@pytest.mark.parametrize("case", ["gemm_small", "gemm_big", "batchnet", "droplet", "lstm_gemm_hid"])
+def test_golden_mlps_on_tensor_cores(case, monkeypatch):
+    monkeypatch.setenv("ROSENNA_MLP_PATH", "tc")
+    d = goldens.case_dir(case)
+    api.initialize(d)
+    assert "mlp_tc" in api.plan_description()
+    ins = goldens.inputs(case)
+    out = api.use_model(ins, n=1)[0]
+    assert_close(out, goldens.golden(case), case)
+    n = 1000
+    rng = np.random.default_rng(5)
+    rows = [int(np.prod(s)) // s[b] for s, b in api.input_specs()]
+    xs = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) for r in rows]
+    out = api.use_model_rows(xs)[0]
+    ref = OracleModel(d).run_batched(n, xs, [1] * len(xs), [1])[0]
+    assert_close(out, ref.reshape(out.shape), f"{case} tc n={n}")
