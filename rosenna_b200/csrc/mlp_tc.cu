@@ -36,8 +36,10 @@ namespace {
 constexpr int kBM = 128;                 // samples per tile (UMMA M)
 constexpr int kKC = 32;                  // K per chunk: 32 fp32 = one 128-byte swizzle row
 constexpr int kNMax = 256;               // widest layer (UMMA N)
-constexpr int kThreadsTc = 256;
+constexpr int kThreadsTc = 320;           // warp 0 TMA, warp 1 MMA, warps 2..9 converters (200 regs each: 64,000 of 65,536)
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTCol = 0;             // TMEM cols [0,256): previous layer's activations
+constexpr uint32_t kPCol = 256;           // TMEM cols [256,512): partial sums of column half h at 256+128h
 constexpr uint32_t kBTile = kNMax * 128;  // bytes of one B tile (hi or lo)
 constexpr uint32_t kATile = kBM * 128;    // bytes of one A tile (hi or lo)
 constexpr uint32_t kSmemB = 2 * 2 * kBTile;  // 2 stages x (hi, lo)
@@ -127,6 +129,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// the same without the wait: several loads can be in flight before tmem_wait_ld()
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // K-major operand, 128-byte swizzle: 8-row atoms of 1024 bytes (SBO), rows of
 // 128 bytes; LBO unused for swizzled K-major (set to 16 bytes); version 1.
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
@@ -189,33 +201,31 @@ __device__ __forceinline__ void put_a16(uint8_t *ahi, uint8_t *alo, int r, int k
     }
 }
 
-struct TcSmem {
-    uint8_t *b[2][2];  // [stage][hi, lo]
-    uint8_t *a[2][2];
-    float *bias;
-    uint64_t *b_full, *b_empty, *a_full, *a_empty, *acc_full, *drain;
-    uint32_t *tmem_slot;
-};
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])));
+}
 
-__global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
+// Which converter group (column half) stages A chunk c of layer l: the input
+// layer alternates; hidden layers read chunk c from the half holding its columns.
+__device__ __forceinline__ int a_owner(int l, int c) { return l == 0 ? (c & 1) : (c >> 2); }
+
+__global__ void __maxnreg__(200) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
-    TcSmem S;
-    for (int s = 0; s < 2; s++) {
-        S.b[s][0] = base + s * 2 * kBTile;
-        S.b[s][1] = S.b[s][0] + kBTile;
-        S.a[s][0] = base + kSmemB + s * 2 * kATile;
-        S.a[s][1] = S.a[s][0] + kATile;
-    }
-    S.bias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias);
-    S.b_full = bars;
-    S.b_empty = bars + 2;
-    S.a_full = bars + 4;
-    S.a_empty = bars + 6;
-    S.acc_full = bars + 8;
-    S.drain = bars + 10;
-    S.tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+    uint8_t *const b0 = base;                   // B stage s: hi at b0 + s*2*kBTile, lo + kBTile
+    uint8_t *const a0 = base + kSmemB;          // A stage s: hi at a0 + s*2*kATile, lo + kATile
+    float *const sbias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias);
+    uint64_t *const b_full = bars, *const b_empty = bars + 2, *const a_full = bars + 4, *const a_empty = bars + 6;
+    uint64_t *const p_full = bars + 8, *const p_empty = bars + 10, *const drain = bars + 12;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nl = p.nlayers;
@@ -223,28 +233,29 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
 
     for (int i = tid; i < nl * kNMax; i += kThreadsTc) {
         const int l = i / kNMax, j = i - l * kNMax;
-        S.bias[i] = j < p.L[l].Np ? p.arena[p.L[l].b_off + j] : 0.f;
+        sbias[i] = j < p.L[l].Np ? p.arena[p.L[l].b_off + j] : 0.f;
     }
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
-            mbar_init(&S.b_full[s], 1);
-            mbar_init(&S.b_empty[s], 1);
-            mbar_init(&S.a_full[s], kBM);
-            mbar_init(&S.a_empty[s], 1);
-            mbar_init(&S.acc_full[s], 1);
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+            mbar_init(&a_full[s], kBM);
+            mbar_init(&a_empty[s], 1);
+            mbar_init(&p_full[s], 1);
+            mbar_init(&p_empty[s], kBM);
         }
-        mbar_init(S.drain, 1);
+        mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(S.tmem_slot)),
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *S.tmem_slot;
+    const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
@@ -255,123 +266,162 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             for (int l = 0; l < nl && ok; l++)
                 for (int c = 0; c < p.L[l].nch && ok; c++, i++) {
                     const int s = i & 1;
-                    const uint32_t use = i >> 1;
-                    if (!(ok = mbar_wait(&S.b_empty[s], (use & 1) ^ 1, p.err, 1))) break;
-                    mbar_arrive_expect_tx(&S.b_full[s], 2u * (uint32_t)p.L[l].Np * 128u);
-                    tma_load_2d(S.b[s][0], &p.maps[l], &S.b_full[s], c * kKC, 0);
-                    tma_load_2d(S.b[s][1], &p.maps[l], &S.b_full[s], c * kKC, p.L[l].Np);
+                    if (!(ok = mbar_wait(&b_empty[s], ((i >> 1) & 1) ^ 1, p.err, 1))) break;
+                    mbar_arrive_expect_tx(&b_full[s], 2u * (uint32_t)p.L[l].Np * 128u);
+                    tma_load_2d(b0 + s * 2 * kBTile, &p.maps[l], &b_full[s], c * kKC, 0);
+                    tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
                 }
-        // our copies in flight: wait until the last loads of each stage have landed
-        for (uint32_t k = (i > 2 ? i - 2 : 0); k < i; k++) {
-            const int s = k & 1;
-            mbar_wait(&S.b_full[s], (k >> 1) & 1, p.err, 0);
-        }
+        // copies still in flight land before the CTA may exit
+        for (uint32_t k = (i > 2 ? i - 2 : 0); k < i; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
-        uint32_t ib = 0, ia = 0;
+        // per chunk of 32 K: two partials of 16 K per column half, each started fresh
+        // (the partials are summed in fp32 registers by the converters)
+        uint32_t ib = 0, ia = 0, pu[2] = {0, 0};
         bool ok = true;
         for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
             for (int l = 0; l < nl && ok; l++) {
-                const uint32_t d = tmem + (uint32_t)((l & 1) * kNMax);
-                const uint32_t idesc = idesc_tf32(p.L[l].Np);
-                for (int c = 0; c < p.L[l].nch; c++, ib++, ia++) {
+                const int Np = p.L[l].Np, nh = (Np + 127) >> 7;
+                for (int c = 0; c < p.L[l].nch && ok; c++, ib++, ia++) {
                     const int sb = ib & 1, sa = ia & 1;
-                    if (!(ok = mbar_wait(&S.b_full[sb], (ib >> 1) & 1, p.err, 2))) break;
-                    if (!(ok = mbar_wait(&S.a_full[sa], (ia >> 1) & 1, p.err, 3))) break;
+                    if (!(ok = mbar_wait(&b_full[sb], (ib >> 1) & 1, p.err, 2))) break;
+                    if (!(ok = mbar_wait(&a_full[sa], (ia >> 1) & 1, p.err, 3))) break;
                     tc_fence_after();
-                    const uint64_t ah = desc_kmajor_sw128(smem_u32(S.a[sa][0]));
-                    const uint64_t al = desc_kmajor_sw128(smem_u32(S.a[sa][1]));
-                    const uint64_t bh = desc_kmajor_sw128(smem_u32(S.b[sb][0]));
-                    const uint64_t bl = desc_kmajor_sw128(smem_u32(S.b[sb][1]));
+                    const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + sa * 2 * kATile));
+                    const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + sa * 2 * kATile + kATile));
+                    const uint64_t bh = desc_kmajor_sw128(smem_u32(b0 + sb * 2 * kBTile));
+                    const uint64_t bl = desc_kmajor_sw128(smem_u32(b0 + sb * 2 * kBTile + kBTile));
+                    for (int sub = 0; sub < 2 && ok; sub++)
+                        for (int h = 0; h < nh && ok; h++) {
+                            const int Nh = min(128, Np - 128 * h);
+                            if (!(ok = mbar_wait(&p_empty[h], (pu[h] & 1) ^ 1, p.err, 4))) break;
+                            tc_fence_after();
+                            const uint32_t d = tmem + kPCol + (uint32_t)(128 * h);
+                            const uint32_t idesc = idesc_tf32(Nh);
+                            const uint64_t boff = (uint64_t)(h * 128 * 128) >> 4;  // rows 128h.. of the B tiles
 #pragma unroll
-                    for (int kk = 0; kk < kKC / 8; kk++) {
-                        const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
-                        umma_tf32(d, al + adv, bh + adv, idesc, (c | kk) != 0);
-                        umma_tf32(d, ah + adv, bl + adv, idesc, 1);
-                        umma_tf32(d, ah + adv, bh + adv, idesc, 1);
-                    }
-                    umma_commit(&S.a_empty[sa]);
-                    umma_commit(&S.b_empty[sb]);
+                            for (int kq = 0; kq < 2; kq++) {
+                                const int kk = 2 * sub + kq;
+                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
+                                umma_tf32(d, al + adv, bh + boff + adv, idesc, kq);
+                                umma_tf32(d, ah + adv, bl + boff + adv, idesc, 1);
+                                umma_tf32(d, ah + adv, bh + boff + adv, idesc, 1);
+                            }
+                            umma_commit(&p_full[h]);
+                            pu[h]++;
+                        }
+                    if (!ok) break;
+                    umma_commit(&a_empty[sa]);
+                    umma_commit(&b_empty[sb]);
                 }
-                if (ok) umma_commit(&S.acc_full[l & 1]);
             }
         // drain: every MMA issued above has completed before TMEM is freed
-        umma_commit(S.drain);
-        mbar_wait(S.drain, 0, p.err, 0);
-    } else if (warp >= 4) {
-        // ---------------- converters / epilogue ----------------
-        const int r = tid - 128;  // sample row in the tile == TMEM lane
-        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        uint32_t ia = 0;
-        uint32_t acc_use[2] = {0, 0};
+        umma_commit(drain);
+        mbar_wait(drain, 0, p.err, 0);
+    } else if (warp >= 2) {
+        // ---------------- converters: group g owns output columns [128g, 128g+128) ----------------
+        const int g = (warp - 2) >> 2, quad = warp & 3;
+        const int r = quad * 32 + lane;  // sample row in the tile == TMEM lane
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        uint32_t ia = 0, pu = 0;
         bool ok = true;
-        for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            const long long n0 = t * kBM;
-            const bool valid = n0 + r < p.n;
-            // layer 0: the input tile, K0 features of sample r
-            for (int c = 0; c < p.L[0].nch && ok; c++, ia++) {
-                const int sa = ia & 1;
-                float v[2][16];
-#pragma unroll
-                for (int h = 0; h < 2; h++)
+        float acc[128];
+
+        // stage A chunk c of layer l into ring slot j
+        auto produce = [&](long long n0, bool valid, int l, int c, uint32_t j) -> bool {
+            const int sa = j & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[sa], ((j >> 1) & 1) ^ 1, p.err, 5))) return false;
+            uint8_t *ahi = a0 + sa * 2 * kATile;
+#pragma unroll 1
+            for (int h = 0; h < 2; h++) {
+                float v[16];
+                if (l == 0) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
                         const int k = c * kKC + h * 16 + e;
-                        v[h][e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + n0 + r) : 0.f;
+                        v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + n0 + r) : 0.f;
                     }
-                ok = __all_sync(0xffffffffu, mbar_wait(&S.a_empty[sa], ((ia >> 1) & 1) ^ 1, p.err, 4));
-                if (!ok) break;
-                put_a16(S.a[sa][0], S.a[sa][1], r, 0, v[0]);
-                put_a16(S.a[sa][0], S.a[sa][1], r, 16, v[1]);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&S.a_full[sa]);
+                } else {
+                    tmem_ld16(lane_base + kTCol + (uint32_t)(c * kKC + h * 16), v);
+                }
+                put_a16(ahi, ahi + kATile, r, h * 16, v);
             }
-            // layers 1..L-1: A chunks from the previous accumulator
-            for (int l = 1; l < nl && ok; l++) {
-                const int pb = (l - 1) & 1;
-                ok = __all_sync(0xffffffffu, mbar_wait(&S.acc_full[pb], acc_use[pb] & 1, p.err, 5));
-                if (!ok) break;
-                acc_use[pb]++;
-                tc_fence_after();
-                const int Nprev = p.L[l - 1].N, actp = p.L[l - 1].act;
-                const float *bias = S.bias + (l - 1) * kNMax;
-                for (int c = 0; c < p.L[l].nch && ok; c++, ia++) {
-                    const int sa = ia & 1;
-                    ok = __all_sync(0xffffffffu, mbar_wait(&S.a_empty[sa], ((ia >> 1) & 1) ^ 1, p.err, 6));
-                    if (!ok) break;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(&a_full[sa]);
+            return true;
+        };
+        // add one partial of this group's column half into acc
+        auto drain_partial = [&](int Np) -> bool {
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6))) return false;
+            tc_fence_after();
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const int col = c * kKC + h * 16;
-                        float v[16];
-                        tmem_ld16(lane_base + (uint32_t)(pb * kNMax + col), v);
+            for (int q = 0; q < 8; q += 2) {
+                if (128 * g + 16 * q < Np) {  // Np is a multiple of 16: pairs may be half used
+                    uint32_t v0[16], v1[16];
+                    const bool two = 128 * g + 16 * (q + 1) < Np;
+                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * q), v0);
+                    if (two) tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * q + 16), v1);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 16; e++)
-                            v[e] = (col + e < Nprev) ? tc_act(v[e] + bias[col + e], actp) : 0.f;
-                        put_a16(S.a[sa][0], S.a[sa][1], r, h * 16, v);
+                    for (int e = 0; e < 16; e++) acc[16 * q + e] += __uint_as_float(v0[e]);
+                    if (two) {
+#pragma unroll
+                        for (int e = 0; e < 16; e++) acc[16 * q + 16 + e] += __uint_as_float(v1[e]);
                     }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    tc_fence_before();
-                    mbar_arrive(&S.a_full[sa]);
                 }
             }
-            if (!ok) break;
-            // epilogue: last layer's accumulator -> outputs
-            const int lb = (nl - 1) & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(&S.acc_full[lb], acc_use[lb] & 1, p.err, 7));
-            if (!ok) break;
-            acc_use[lb]++;
-            tc_fence_after();
-            const int Nl = p.L[nl - 1].N, actl = p.L[nl - 1].act;
-            const float *bias = S.bias + (nl - 1) * kNMax;
-            for (int col = 0; col < p.L[nl - 1].Np; col += 16) {
-                float v[16];
-                tmem_ld16(lane_base + (uint32_t)(lb * kNMax + col), v);
-#pragma unroll
-                for (int e = 0; e < 16; e++)
-                    if (valid && col + e < Nl)
-                        p.out[(long long)(col + e) * p.ld_out + n0 + r] = tc_act(v[e] + bias[col + e], actl);
-            }
             tc_fence_before();
+            mbar_arrive(&p_empty[g]);
+            pu++;
+            return true;
+        };
+
+        for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const long long n0 = t * kBM;
+            const bool valid = n0 + r < p.n;
+            for (int l = 0; l < nl && ok; l++) {
+                const int nch = p.L[l].nch, Np = p.L[l].Np, N = p.L[l].N, act = p.L[l].act;
+                const bool has_half = 128 * g < Np;
+#pragma unroll
+                for (int q = 0; q < 128; q++) acc[q] = 0.f;
+                for (int c = 0; c < 2 && c < nch && ok; c++)
+                    if (a_owner(l, c) == g) ok = produce(n0, valid, l, c, ia + c);
+                for (int c = 0; c < nch && ok; c++) {
+                    if (has_half) {
+                        ok = drain_partial(Np);
+                        if (ok) ok = drain_partial(Np);
+                    }
+                    if (ok && c + 2 < nch && a_owner(l, c + 2) == g) ok = produce(n0, valid, l, c + 2, ia + c + 2);
+                }
+                ia += nch;
+                if (!ok || !has_half) continue;
+                // bias + activation of this half; into T for the next layer, or out
+                const float *bias = sbias + l * kNMax + 128 * g;
+                if (l + 1 < nl) {
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        float v[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            const int col = 128 * g + 16 * q + e;
+                            v[e] = col < N ? tc_act(acc[16 * q + e] + bias[16 * q + e], act) : 0.f;
+                        }
+                        tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                } else if (valid) {
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            const int col = 128 * g + 16 * q + e;
+                            if (col < N)
+                                p.out[(long long)col * p.ld_out + n0 + r] =
+                                    tc_act(acc[16 * q + e] + bias[16 * q + e], act);
+                        }
+                }
+            }
         }
     }
     tc_fence_before();
