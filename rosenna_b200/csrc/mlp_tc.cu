@@ -356,19 +356,12 @@ __global__ void __maxnreg__(200) mlp_tc_kernel(const __grid_constant__ TcArgs p)
             if (!__all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6))) return false;
             tc_fence_after();
 #pragma unroll
-            for (int q = 0; q < 8; q += 2) {
-                if (128 * g + 16 * q < Np) {  // Np is a multiple of 16: pairs may be half used
-                    uint32_t v0[16], v1[16];
-                    const bool two = 128 * g + 16 * (q + 1) < Np;
-                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * q), v0);
-                    if (two) tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * q + 16), v1);
-                    tmem_wait_ld();
+            for (int q = 0; q < 8; q++) {
+                if (128 * g + 16 * q < Np) {
+                    float v[16];
+                    tmem_ld16(lane_base + kPCol + (uint32_t)(128 * g + 16 * q), v);
 #pragma unroll
-                    for (int e = 0; e < 16; e++) acc[16 * q + e] += __uint_as_float(v0[e]);
-                    if (two) {
-#pragma unroll
-                        for (int e = 0; e < 16; e++) acc[16 * q + 16 + e] += __uint_as_float(v1[e]);
-                    }
+                    for (int e = 0; e < 16; e++) acc[16 * q + e] += v[e];
                 }
             }
             tc_fence_before();
