@@ -36,7 +36,7 @@ namespace {
 constexpr int kBM = 128;                 // samples per tile (UMMA M)
 constexpr int kKC = 32;                  // K per chunk: 32 fp32 = one 128-byte swizzle row
 constexpr int kNMax = 256;               // widest layer (UMMA N)
-constexpr int kThreadsTc = 320;           // warp 0 TMA, warp 1 MMA, warps 2..9 converters (200 regs each: 64,000 of 65,536)
+constexpr int kThreadsTc = 320;           // warp 0 TMA, warp 1 MMA, warps 2..9 converters
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTCol = 0;             // TMEM cols [0,256): previous layer's activations
 constexpr uint32_t kPCol = 256;           // TMEM cols [256,512): partial sums of column half h at 256+128h
@@ -129,16 +129,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// the same without the wait: several loads can be in flight before tmem_wait_ld()
-__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 // K-major operand, 128-byte swizzle: 8-row atoms of 1024 bytes (SBO), rows of
 // 128 bytes; LBO unused for swizzled K-major (set to 16 bytes); version 1.
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
@@ -216,7 +206,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 // layer alternates; hidden layers read chunk c from the half holding its columns.
 __device__ __forceinline__ int a_owner(int l, int c) { return l == 0 ? (c & 1) : (c >> 2); }
 
-__global__ void __maxnreg__(200) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
+__global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *const b0 = base;                   // B stage s: hi at b0 + s*2*kBTile, lo + kBTile
