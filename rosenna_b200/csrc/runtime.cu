@@ -189,7 +189,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                         launches++;
                     }
                     if (e == cudaSuccess)
-                        e = cudaMemcpyAsync(d.err_host, d.err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+                        e = cudaMemcpyAsync(d.err_host, d.err, 8 * sizeof(int), cudaMemcpyDeviceToHost, stream);
                     break;
                 }
                 MlpArgs a{};
@@ -278,11 +278,19 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
 
 // A tensor-core kernel that timed out leaves a code in its status word; the
 // engine then refuses further calls until it is initialized again.
+std::string tc_error_text(const int *e) {
+    char buf[256];
+    snprintf(buf, sizeof buf,
+             "a tensor-core kernel timed out waiting on its pipeline (wait %d, block %d, thread %d, at 0x%x, "
+             "parity %d, counters %d %d)",
+             e[0], e[1], e[2], e[3], e[4], e[5], e[6]);
+    return buf;
+}
+
 Status check_device_status() {
     for (auto &d : g_ctx.devs)
         if (d->err_host && *(volatile int *)d->err_host)
-            return Status::Err(ROSENNA_ERR_CUDA, "a tensor-core kernel timed out waiting on its pipeline (code " +
-                                                     std::to_string(*d->err_host) + "); re-run initialize()");
+            return Status::Err(ROSENNA_ERR_CUDA, tc_error_text(d->err_host) + "; re-run initialize()");
     return Status::Ok();
 }
 
@@ -343,8 +351,7 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
     }
     for (auto &s : d.slots) CUDA_TRY(cudaStreamSynchronize(s.stream));
     CUDA_TRY(cudaGetLastError());
-    if (d.err_host && *(volatile int *)d.err_host)
-        return Status::Err(ROSENNA_ERR_CUDA, "a tensor-core kernel timed out waiting on its pipeline");
+    if (d.err_host && *(volatile int *)d.err_host) return Status::Err(ROSENNA_ERR_CUDA, tc_error_text(d.err_host));
     return Status::Ok();
 }
 
@@ -423,10 +430,10 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         CUDA_TRY(mlp_tc_configure());
         CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
         CUDA_TRY(cudaMemcpy(d->arena, P.arena.data(), sizeof(float) * P.arena.size(), cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMalloc(&d->err, sizeof(int)));
-        CUDA_TRY(cudaMemset(d->err, 0, sizeof(int)));
-        CUDA_TRY(cudaMallocHost(&d->err_host, sizeof(int)));
-        *d->err_host = 0;
+        CUDA_TRY(cudaMalloc(&d->err, 8 * sizeof(int)));
+        CUDA_TRY(cudaMemset(d->err, 0, 8 * sizeof(int)));
+        CUDA_TRY(cudaMallocHost(&d->err_host, 8 * sizeof(int)));
+        std::memset(d->err_host, 0, 8 * sizeof(int));
         d->tc_args.assign(P.steps.size(), TcArgs{});
         for (size_t si = 0; si < P.steps.size(); si++) {
             const Step &s = P.steps[si];
