@@ -80,25 +80,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 // Bounded wait for the phase of `parity` to complete.  Gives up (returns false)
 // after kWaitNs / kWaitIters, or as soon as another role has recorded an error.
-// The first thread to give up records err[0] = code and, in err[1..7], where it
-// waited: block, thread, `where` (caller state), parity, and two counters.
+// The first thread to give up records err[0] = code and, in err[1..6], where it
+// waited: block, thread, `where` (caller state), parity and two counters.  A
+// thread passing `slot` > 0 also records its own state in err[8*slot ..] when
+// it gives up for any reason (block 0 only), so every role's position is known.
 __device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code, int where = 0,
-                                       int c1 = 0, int c2 = 0) {
+                                       int c1 = 0, int c2 = 0, int slot = 0) {
     const uint64_t t0 = globaltimer();
+    bool other = false;
     for (uint32_t i = 0; i < kWaitIters; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*(volatile int *)err) return false;
+        if (*(volatile int *)err) {
+            other = true;
+            break;
+        }
         if ((i & 255) == 255 && globaltimer() - t0 > kWaitNs) break;
     }
-    if (code != 0 && atomicCAS(err, 0, code) == 0) {
+    if (!other && code != 0 && atomicCAS(err, 0, code) == 0) {
         err[1] = blockIdx.x;
         err[2] = threadIdx.x;
         err[3] = where;
         err[4] = (int)parity;
         err[5] = c1;
         err[6] = c2;
-        __threadfence();
     }
+    if (slot > 0 && blockIdx.x == 0) {
+        int *e = err + 8 * slot;
+        e[0] = code;
+        e[1] = where;
+        e[2] = (int)parity;
+        e[3] = c1;
+        e[4] = c2;
+        e[5] = (int)(globaltimer() - t0 > kWaitNs);
+    }
+    __threadfence();
     return false;
 }
 
@@ -267,7 +282,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             for (int l = 0; l < nl && ok; l++)
                 for (int c = 0; c < p.L[l].nch && ok; c++, i++) {
                     const int s = i & 1;
-                    if (!(ok = mbar_wait(&b_empty[s], ((i >> 1) & 1) ^ 1, p.err, 1, (l << 8) | c, (int)i))) break;
+                    if (!(ok = mbar_wait(&b_empty[s], ((i >> 1) & 1) ^ 1, p.err, 1, (l << 8) | c, (int)i, 0, 1))) break;
                     mbar_arrive_expect_tx(&b_full[s], 2u * (uint32_t)p.L[l].Np * 128u);
                     tma_load_2d(b0 + s * 2 * kBTile, &p.maps[l], &b_full[s], c * kKC, 0);
                     tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
@@ -285,8 +300,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                 const int Np = p.L[l].Np, nh = (Np + 127) >> 7;
                 for (int c = 0; c < p.L[l].nch && ok; c++, ib++, ia++) {
                     const int sb = ib & 1, sa = ia & 1;
-                    if (!(ok = mbar_wait(&b_full[sb], (ib >> 1) & 1, p.err, 2, (l << 8) | c, (int)ib))) break;
-                    if (!(ok = mbar_wait(&a_full[sa], (ia >> 1) & 1, p.err, 3, (l << 8) | c, (int)ia))) break;
+                    if (!(ok = mbar_wait(&b_full[sb], (ib >> 1) & 1, p.err, 2, (l << 8) | c, (int)ib, 0, 2))) break;
+                    if (!(ok = mbar_wait(&a_full[sa], (ia >> 1) & 1, p.err, 3, (l << 8) | c, (int)ia, 0, 2))) break;
                     tc_fence_after();
                     const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + sa * 2 * kATile));
                     const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + sa * 2 * kATile + kATile));
@@ -296,7 +311,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                         for (int h = 0; h < nh && ok; h++) {
                             const int Nh = min(128, Np - 128 * h);
                             if (!(ok = mbar_wait(&p_empty[h], (pu[h] & 1) ^ 1, p.err, 4, (l << 16) | (c << 8) | (sub << 4) | h,
-                                                 (int)pu[h], (int)ia)))
+                                                 (int)pu[h], (int)ia, 2)))
                                 break;
                             tc_fence_after();
                             const uint32_t d = tmem + kPCol + (uint32_t)(128 * h);
@@ -333,7 +348,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         // stage A chunk c of layer l into ring slot j
         auto produce = [&](long long n0, bool valid, int l, int c, uint32_t j) -> bool {
             const int sa = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[sa], ((j >> 1) & 1) ^ 1, p.err, 5, (l << 8) | c, (int)j, g)))
+            if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[sa], ((j >> 1) & 1) ^ 1, p.err, 5, (l << 8) | c, (int)j,
+                                                   (int)pu, (lane == 0 && quad == 2) ? 3 + g : 0)))
                 return false;
             uint8_t *ahi = a0 + sa * 2 * kATile;
 #pragma unroll 1
@@ -357,7 +373,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         };
         // add one partial of this group's column half into acc
         auto drain_partial = [&](int Np, int where) -> bool {
-            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, where, (int)pu, g))) return false;
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, where, (int)pu, (int)ia,
+                                                   (lane == 0 && quad == 2) ? 3 + g : 0)))
+                return false;
             tc_fence_after();
 #pragma unroll
             for (int q = 0; q < 8; q++) {

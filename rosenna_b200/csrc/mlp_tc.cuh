@@ -25,7 +25,7 @@ struct TcArgs {
     float *out;
     long long ld_out;
     long long n;
-    int *err;  // [8]: err[0] = non-zero code when a wait times out, err[1..6] where
+    int *err;  // [64]: err[0] = non-zero code when a wait times out, err[1..6] where, err[8r..] per role
     int nlayers;
     TcLayer L[kTcMaxLayers];
 };

@@ -189,7 +189,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                         launches++;
                     }
                     if (e == cudaSuccess)
-                        e = cudaMemcpyAsync(d.err_host, d.err, 8 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
                     break;
                 }
                 MlpArgs a{};
@@ -279,11 +279,18 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
 // A tensor-core kernel that timed out leaves a code in its status word; the
 // engine then refuses further calls until it is initialized again.
 std::string tc_error_text(const int *e) {
-    char buf[256];
-    snprintf(buf, sizeof buf,
-             "a tensor-core kernel timed out waiting on its pipeline (wait %d, block %d, thread %d, at 0x%x, "
-             "parity %d, counters %d %d)",
-             e[0], e[1], e[2], e[3], e[4], e[5], e[6]);
+    char buf[768];
+    int k = snprintf(buf, sizeof buf,
+                     "a tensor-core kernel timed out waiting on its pipeline (wait %d, block %d, thread %d, at 0x%x, "
+                     "parity %d, counters %d %d)",
+                     e[0], e[1], e[2], e[3], e[4], e[5], e[6]);
+    static const char *role[] = {"", "tma", "mma", "conv0", "conv1"};
+    for (int r = 1; r <= 4 && k < (int)sizeof buf; r++) {
+        const int *s = e + 8 * r;
+        if (s[0] == 0 && s[1] == 0 && s[3] == 0) continue;
+        k += snprintf(buf + k, sizeof buf - (size_t)k, "; %s: wait %d at 0x%x parity %d counters %d %d%s", role[r], s[0],
+                      s[1], s[2], s[3], s[4], s[5] ? " (timed out)" : "");
+    }
     return buf;
 }
 
@@ -430,10 +437,10 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         CUDA_TRY(mlp_tc_configure());
         CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
         CUDA_TRY(cudaMemcpy(d->arena, P.arena.data(), sizeof(float) * P.arena.size(), cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMalloc(&d->err, 8 * sizeof(int)));
-        CUDA_TRY(cudaMemset(d->err, 0, 8 * sizeof(int)));
-        CUDA_TRY(cudaMallocHost(&d->err_host, 8 * sizeof(int)));
-        std::memset(d->err_host, 0, 8 * sizeof(int));
+        CUDA_TRY(cudaMalloc(&d->err, 64 * sizeof(int)));
+        CUDA_TRY(cudaMemset(d->err, 0, 64 * sizeof(int)));
+        CUDA_TRY(cudaMallocHost(&d->err_host, 64 * sizeof(int)));
+        std::memset(d->err_host, 0, 64 * sizeof(int));
         d->tc_args.assign(P.steps.size(), TcArgs{});
         for (size_t si = 0; si < P.steps.size(); si++) {
             const Step &s = P.steps[si];
