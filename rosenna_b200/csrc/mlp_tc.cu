@@ -342,22 +342,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         const int r = quad * 32 + lane;  // sample row in the tile == TMEM lane
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
         uint32_t ia = 0, pu = 0;
-        // phases of each A slot's a_empty barrier this thread has seen complete: a
-        // group may skip the other group's chunks, so it confirms them in order
-        // (a parity test more than one phase ahead would alias)
-        uint32_t a_conf[2] = {0, 0};
         bool ok = true;
         float acc[128];
 
+        // Every converter thread observes the consumption of every A chunk, in
+        // order (both groups, whoever staged the chunk): each a_empty phase is then
+        // awaited by a thread that has seen the phase before it, so the parity
+        // test cannot alias.  Chunk j's slot is free again once chunk j is seen.
+        auto wait_a_consumed = [&](int l, int c, uint32_t j) -> bool {
+            return __all_sync(0xffffffffu, mbar_wait(&a_empty[j & 1], (j >> 1) & 1, p.err, 5, (l << 8) | c, (int)j,
+                                                     (int)pu, (lane == 0 && quad == 2) ? 3 + g : 0));
+        };
+
         // stage A chunk c of layer l into ring slot j
         auto produce = [&](long long n0, bool valid, int l, int c, uint32_t j) -> bool {
-            const int sa = j & 1;
-            while (a_conf[sa] < (j >> 1)) {  // use j>>1 of this slot needs phases 0 .. (j>>1)-1 complete
-                if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[sa], a_conf[sa] & 1, p.err, 5, (l << 8) | c, (int)j,
-                                                       (int)a_conf[sa], (lane == 0 && quad == 2) ? 3 + g : 0)))
-                    return false;
-                a_conf[sa]++;
-            }
+            const int sa = j & 1;  // free: chunk j-2 of this slot was seen consumed
             uint8_t *ahi = a0 + sa * 2 * kATile;
 #pragma unroll 1
             for (int h = 0; h < 2; h++) {
@@ -414,6 +413,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                         ok = drain_partial(Np, (l << 16) | (c << 8));
                         if (ok) ok = drain_partial(Np, (l << 16) | (c << 8) | 16);
                     }
+                    if (ok) ok = wait_a_consumed(l, c, ia + c);
                     if (ok && c + 2 < nch && a_owner(l, c + 2) == g) ok = produce(n0, valid, l, c + 2, ia + c + 2);
                 }
                 ia += nch;
