@@ -84,8 +84,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // waited: block, thread, `where` (caller state), parity and two counters.  A
 // thread passing `slot` > 0 also records its own state in err[8*slot ..] when
 // it gives up for any reason (block 0 only), so every role's position is known.
-__device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code, int where = 0,
-                                       int c1 = 0, int c2 = 0, int slot = 0) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code, int where = 0,
+                                          int c1 = 0, int c2 = 0, int slot = 0) {
+    if (mbar_try_wait(bar, parity)) return true;  // fast path
     const uint64_t t0 = globaltimer();
     bool other = false;
     for (uint32_t i = 0; i < kWaitIters; i++) {
@@ -232,6 +233,34 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 // layer alternates; hidden layers read chunk c from the half holding its columns.
 __device__ __forceinline__ int a_owner(int l, int c) { return l == 0 ? (c & 1) : (c >> 2); }
 
+// Stages A chunk c of layer l (tile t) into A ring slot j&1 for this thread's
+// row: the input layer from global memory, hidden layers from TMEM (the
+// previous layer's activations), split into tf32 hi/lo, 128-byte swizzled.
+// The slot is known free (chunk j-2 was seen consumed).
+__device__ __forceinline__ void stage_a(const TcArgs &p, uint8_t *a0, uint32_t lane_base, int r, int t, int l, int c,
+                                        uint32_t j) {
+    uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
+#pragma unroll 1
+    for (int h = 0; h < 2; h++) {
+        float v[16];
+        if (l == 0) {
+            const long long row = (long long)t * kBM + r;
+            const bool valid = row < p.n;
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                const int k = c * kKC + h * 16 + e;
+                v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + row) : 0.f;
+            }
+        } else {
+            tmem_ld16(lane_base + kTCol + (uint32_t)(c * kKC + h * 16), v);
+        }
+        put_a16(ahi, ahi + kATile, r, h * 16, v);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    mbar_arrive(reinterpret_cast<uint64_t *>(a0 + kSmemA + kSmemBias) + 4 + (j & 1));  // a_full[j & 1]
+}
+
 __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
@@ -341,85 +370,56 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         const int g = (warp - 2) >> 2, quad = warp & 3;
         const int r = quad * 32 + lane;  // sample row in the tile == TMEM lane
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;  // diagnostics of this group
         uint32_t ia = 0, pu = 0;
         bool ok = true;
         float acc[128];
-
-        // Every converter thread observes the consumption of every A chunk, in
-        // order (both groups, whoever staged the chunk): each a_empty phase is then
-        // awaited by a thread that has seen the phase before it, so the parity
-        // test cannot alias.  Chunk j's slot is free again once chunk j is seen.
-        auto wait_a_consumed = [&](int l, int c, uint32_t j) -> bool {
-            return __all_sync(0xffffffffu, mbar_wait(&a_empty[j & 1], (j >> 1) & 1, p.err, 5, (l << 8) | c, (int)j,
-                                                     (int)pu, (lane == 0 && quad == 2) ? 3 + g : 0));
-        };
-
-        // stage A chunk c of layer l into ring slot j
-        auto produce = [&](long long n0, bool valid, int l, int c, uint32_t j) -> bool {
-            const int sa = j & 1;  // free: chunk j-2 of this slot was seen consumed
-            uint8_t *ahi = a0 + sa * 2 * kATile;
-#pragma unroll 1
-            for (int h = 0; h < 2; h++) {
-                float v[16];
-                if (l == 0) {
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const int k = c * kKC + h * 16 + e;
-                        v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + n0 + r) : 0.f;
-                    }
-                } else {
-                    tmem_ld16(lane_base + kTCol + (uint32_t)(c * kKC + h * 16), v);
-                }
-                put_a16(ahi, ahi + kATile, r, h * 16, v);
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc_fence_before();
-            mbar_arrive(&a_full[sa]);
-            return true;
-        };
-        // add one partial of this group's column half into acc
-        auto drain_partial = [&](int Np, int where) -> bool {
-            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, where, (int)pu, (int)ia,
-                                                   (lane == 0 && quad == 2) ? 3 + g : 0)))
-                return false;
-            tc_fence_after();
-#pragma unroll
-            for (int q = 0; q < 8; q++) {
-                if (128 * g + 16 * q < Np) {
-                    float v[16];
-                    tmem_ld16(lane_base + kPCol + (uint32_t)(128 * g + 16 * q), v);
-#pragma unroll
-                    for (int e = 0; e < 16; e++) acc[16 * q + e] += v[e];
-                }
-            }
-            tc_fence_before();
-            mbar_arrive(&p_empty[g]);
-            pu++;
-            return true;
-        };
-
-        for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            const long long n0 = t * kBM;
-            const bool valid = n0 + r < p.n;
+        for (int t = blockIdx.x; t < (int)ntiles && ok; t += gridDim.x) {
             for (int l = 0; l < nl && ok; l++) {
-                const int nch = p.L[l].nch, Np = p.L[l].Np, N = p.L[l].N, act = p.L[l].act;
-                const bool has_half = 128 * g < Np;
+                const int nch = p.L[l].nch;
+                const bool has_half = 128 * g < p.L[l].Np;
 #pragma unroll
                 for (int q = 0; q < 128; q++) acc[q] = 0.f;
-                for (int c = 0; c < 2 && c < nch && ok; c++)
-                    if (a_owner(l, c) == g) ok = produce(n0, valid, l, c, ia + c);
+                if (a_owner(l, 0) == g) stage_a(p, a0, lane_base, r, t, l, 0, ia);
+                if (nch > 1 && a_owner(l, 1) == g) stage_a(p, a0, lane_base, r, t, l, 1, ia + 1);
                 for (int c = 0; c < nch && ok; c++) {
                     if (has_half) {
-                        ok = drain_partial(Np, (l << 16) | (c << 8));
-                        if (ok) ok = drain_partial(Np, (l << 16) | (c << 8) | 16);
+#pragma unroll 1
+                        for (int sub = 0; sub < 2 && ok; sub++) {
+                            // one 16-deep partial of this half: add it into acc
+                            ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 16) | (c << 8) | sub,
+                                                                   (int)pu, (int)ia, slot));
+                            if (!ok) break;
+                            tc_fence_after();
+                            const int Np = p.L[l].Np;
+#pragma unroll
+                            for (int q = 0; q < 8; q++) {
+                                if (128 * g + 16 * q < Np) {
+                                    float v[16];
+                                    tmem_ld16(lane_base + kPCol + (uint32_t)(128 * g + 16 * q), v);
+#pragma unroll
+                                    for (int e = 0; e < 16; e++) acc[16 * q + e] += v[e];
+                                }
+                            }
+                            tc_fence_before();
+                            mbar_arrive(&p_empty[g]);
+                            pu++;
+                        }
+                        if (!ok) break;
                     }
-                    if (ok) ok = wait_a_consumed(l, c, ia + c);
-                    if (ok && c + 2 < nch && a_owner(l, c + 2) == g) ok = produce(n0, valid, l, c + 2, ia + c + 2);
+                    // Every converter thread observes the consumption of every A chunk in
+                    // order (whichever group staged it), so each a_empty phase is awaited by
+                    // a thread that has seen the previous one: the parity test cannot alias.
+                    const uint32_t j = ia + (uint32_t)c;
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(&a_empty[j & 1], (j >> 1) & 1, p.err, 5, (l << 8) | c, (int)j, (int)pu, slot));
+                    if (ok && c + 2 < nch && a_owner(l, c + 2) == g) stage_a(p, a0, lane_base, r, t, l, c + 2, j + 2);
                 }
-                ia += nch;
+                ia += (uint32_t)nch;
                 if (!ok || !has_half) continue;
                 // bias + activation of this half; into T for the next layer, or out
                 const float *bias = sbias + l * kNMax + 128 * g;
+                const int N = p.L[l].N, act = p.L[l].act;
                 if (l + 1 < nl) {
 #pragma unroll
                     for (int q = 0; q < 8; q++) {
@@ -432,16 +432,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                         tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
                     }
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                } else if (valid) {
+                } else {
+                    const long long row0 = (long long)t * kBM + r;
+                    if (row0 < p.n) {
+                        float *o = p.out + row0 + (long long)(128 * g) * p.ld_out;
 #pragma unroll
-                    for (int q = 0; q < 8; q++)
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            const int col = 128 * g + 16 * q + e;
-                            if (col < N)
-                                p.out[(long long)col * p.ld_out + n0 + r] =
-                                    tc_act(acc[16 * q + e] + bias[16 * q + e], act);
-                        }
+                        for (int q = 0; q < 128; q++)
+                            if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act(acc[q] + bias[q], act);
+                    }
                 }
             }
         }
