@@ -8,21 +8,24 @@
 // relative), accumulated in fp32 in tensor memory: fp32-level accuracy from
 // the TF32 tensor pipe.
 //
-// Per CTA (one per SM, persistent over tiles of 128 samples):
-//   warp 0, one lane : TMA producer — streams each layer's [Wh | Wl] in K-chunks
-//                      of 32 (128-byte swizzled rows) into a 2-stage ring
-//   warp 1, one lane : MMA issuer — per chunk 4 K-steps x 3 tcgen05.mma
-//                      (M=128 samples, N = layer width, K=8), commits free the
-//                      ring stages; warp 1 also owns the TMEM allocation
-//   warps 4..7       : converters — thread r owns sample r (TMEM lane r): they
-//                      stage the input tile, and between layers read the
-//                      accumulator (tcgen05.ld), add bias, apply the
-//                      activation, split hi/lo and write the next layer's A
-//                      chunk (swizzled, K-major) into a 2-stage ring; the last
-//                      layer's epilogue writes the outputs to global memory
-// Two accumulators of 256 columns alternate between layers (512 TMEM columns).
+// Per CTA (one per SM, persistent over tiles of 128 samples), 8 warps in two
+// groups of four; group g owns output columns [128g, 128g+128) and thread r of a
+// group owns sample row r (TMEM lane r):
+//   - one lane of each group issues that group's tcgen05.mma (M=128 samples,
+//     N=128 columns, K=8; three per K-step for the 3xTF32 split) into its own
+//     TMEM partial buffer, 16 K at a time; the group adds each partial into fp32
+//     registers (round-to-nearest: the tensor core truncates while it
+//     accumulates, so long chains inside TMEM lose accuracy).  While one group
+//     drains, the other group's MMAs run.
+//   - one lane streams [Wh | Wl] K-chunks of 32 (128-byte swizzled rows) by TMA
+//     into a 2-stage ring, two chunks ahead of the MMAs.
+//   - the A operand of layer 0 is the input tile, of later layers the previous
+//     layer's activations (kept in TMEM), split hi/lo into a 2-stage smem ring.
+//   - after the last K-chunk a group adds bias, applies the activation and
+//     writes its half to TMEM for the next layer, or to global memory.
 // Every wait on an mbarrier is bounded; on time-out the kernel records an error
-// code in `err`, drains what it issued, frees TMEM and returns.
+// code and where it waited in `err`, lets every role finish, frees TMEM and
+// returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -36,7 +39,7 @@ namespace {
 constexpr int kBM = 128;                 // samples per tile (UMMA M)
 constexpr int kKC = 32;                  // K per chunk: 32 fp32 = one 128-byte swizzle row
 constexpr int kNMax = 256;               // widest layer (UMMA N)
-constexpr int kThreadsTc = 320;           // warp 0 TMA, warp 1 MMA, warps 2..9 converters
+constexpr int kThreadsTc = 256;           // two groups of four warps (2 warps per SMSP: up to 255 registers)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTCol = 0;             // TMEM cols [0,256): previous layer's activations
 constexpr uint32_t kPCol = 256;           // TMEM cols [256,512): partial sums of column half h at 256+128h
@@ -156,6 +159,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// the same without the wait: several loads in flight before tmem_wait_ld()
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // K-major operand, 128-byte swizzle: 8-row atoms of 1024 bytes (SBO), rows of
 // 128 bytes; LBO unused for swizzled K-major (set to 16 bytes); version 1.
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
@@ -237,8 +250,8 @@ __device__ __forceinline__ int a_owner(int l, int c) { return l == 0 ? (c & 1) :
 // row: the input layer from global memory, hidden layers from TMEM (the
 // previous layer's activations), split into tf32 hi/lo, 128-byte swizzled.
 // The slot is known free (chunk j-2 was seen consumed).
-__device__ __forceinline__ void stage_a(const TcArgs &p, uint8_t *a0, uint32_t lane_base, int r, int t, int l, int c,
-                                        uint32_t j) {
+__device__ __forceinline__ void stage_a(const TcArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base, int r,
+                                        int t, int l, int c, uint32_t j) {
     uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
 #pragma unroll 1
     for (int h = 0; h < 2; h++) {
@@ -258,23 +271,49 @@ __device__ __forceinline__ void stage_a(const TcArgs &p, uint8_t *a0, uint32_t l
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
-    mbar_arrive(reinterpret_cast<uint64_t *>(a0 + kSmemA + kSmemBias) + 4 + (j & 1));  // a_full[j & 1]
+    mbar_arrive(&a_full[j & 1]);
+}
+
+// Global chunk after (t, l, c) by `steps` in this CTA's (tile, layer, chunk) order.
+__device__ __forceinline__ bool chunk_after(const TcArgs &p, int ntiles, int &t, int &l, int &c, int steps) {
+    c += steps;
+    while (c >= p.L[l].nch) {
+        c -= p.L[l].nch;
+        if (++l == p.nlayers) {
+            l = 0;
+            t += gridDim.x;
+            if (t >= ntiles) return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void load_b(const TcArgs &p, uint8_t *b0, uint64_t *b_full, int l, int c, uint32_t j) {
+    const int s = j & 1;
+    mbar_arrive_expect_tx(&b_full[s], 2u * (uint32_t)p.L[l].Np * 128u);
+    tma_load_2d(b0 + s * 2 * kBTile, &p.maps[l], &b_full[s], c * kKC, 0);
+    tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
 }
 
 __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *const b0 = base;                   // B stage s: hi at b0 + s*2*kBTile, lo + kBTile
-    uint8_t *const a0 = base + kSmemB;          // A stage s: hi at a0 + s*2*kATile, lo + kATile
+    uint8_t *const b0 = base;           // B stage s: hi at b0 + s*2*kBTile, lo + kBTile
+    uint8_t *const a0 = base + kSmemB;  // A stage s: hi at a0 + s*2*kATile, lo + kATile
     float *const sbias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
     uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias);
-    uint64_t *const b_full = bars, *const b_empty = bars + 2, *const a_full = bars + 4, *const a_empty = bars + 6;
-    uint64_t *const p_full = bars + 8, *const p_empty = bars + 10, *const drain = bars + 12;
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+    uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
+    uint64_t *const p_full = bars + 6, *const p_empty = bars + 8;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = warp >> 2, quad = warp & 3;
+    const int r = quad * 32 + lane;                    // sample row in the tile == TMEM lane
+    const bool issuer = lane == 0 && quad == 0;        // issues this group's MMAs
+    const bool loader = g == 0 && lane == 0 && quad == 1;  // issues the TMA loads
+    const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;  // records this group's position on error
     const int nl = p.nlayers;
-    const long long ntiles = (p.n + kBM - 1) / kBM;
+    const int ntiles = (int)((p.n + kBM - 1) / kBM);
 
     for (int i = tid; i < nl * kNMax; i += kThreadsTc) {
         const int l = i / kNMax, j = i - l * kNMax;
@@ -283,16 +322,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
-            mbar_init(&b_empty[s], 1);
             mbar_init(&a_full[s], kBM);
-            mbar_init(&a_empty[s], 1);
+            mbar_init(&a_empty[s], 2);  // one tcgen05.commit per group
             mbar_init(&p_full[s], 1);
             mbar_init(&p_empty[s], kBM);
         }
-        mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {
+    if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -301,152 +338,149 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
 
-    if (warp == 0 && lane == 0) {
-        // ---------------- TMA producer ----------------
+    uint32_t b_issued = 0, b_done = 0;  // loader: chunks loaded / seen consumed
+    if (loader) {
         for (int l = 0; l < nl; l++) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.maps[l]) : "memory");
-        uint32_t i = 0;  // chunk counter over (tile, layer, chunk)
-        bool ok = true;
-        for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
-            for (int l = 0; l < nl && ok; l++)
-                for (int c = 0; c < p.L[l].nch && ok; c++, i++) {
-                    const int s = i & 1;
-                    if (!(ok = mbar_wait(&b_empty[s], ((i >> 1) & 1) ^ 1, p.err, 1, (l << 8) | c, (int)i, 0, 1))) break;
-                    mbar_arrive_expect_tx(&b_full[s], 2u * (uint32_t)p.L[l].Np * 128u);
-                    tma_load_2d(b0 + s * 2 * kBTile, &p.maps[l], &b_full[s], c * kKC, 0);
-                    tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
-                }
-        // copies still in flight land before the CTA may exit
-        for (uint32_t k = (i > 2 ? i - 2 : 0); k < i; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
-        // per chunk of 32 K: two partials of 16 K per column half, each started fresh
-        // (the partials are summed in fp32 registers by the converters)
-        uint32_t ib = 0, ia = 0, pu[2] = {0, 0};
-        bool ok = true;
-        for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
-            for (int l = 0; l < nl && ok; l++) {
-                const int Np = p.L[l].Np, nh = (Np + 127) >> 7;
-                for (int c = 0; c < p.L[l].nch && ok; c++, ib++, ia++) {
-                    const int sb = ib & 1, sa = ia & 1;
-                    if (!(ok = mbar_wait(&b_full[sb], (ib >> 1) & 1, p.err, 2, (l << 8) | c, (int)ib, 0, 2))) break;
-                    if (!(ok = mbar_wait(&a_full[sa], (ia >> 1) & 1, p.err, 3, (l << 8) | c, (int)ia, 0, 2))) break;
-                    tc_fence_after();
-                    const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + sa * 2 * kATile));
-                    const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + sa * 2 * kATile + kATile));
-                    const uint64_t bh = desc_kmajor_sw128(smem_u32(b0 + sb * 2 * kBTile));
-                    const uint64_t bl = desc_kmajor_sw128(smem_u32(b0 + sb * 2 * kBTile + kBTile));
-                    for (int sub = 0; sub < 2 && ok; sub++)
-                        for (int h = 0; h < nh && ok; h++) {
-                            const int Nh = min(128, Np - 128 * h);
-                            if (!(ok = mbar_wait(&p_empty[h], (pu[h] & 1) ^ 1, p.err, 4, (l << 16) | (c << 8) | (sub << 4) | h,
-                                                 (int)pu[h], (int)ia, 2)))
-                                break;
-                            tc_fence_after();
-                            const uint32_t d = tmem + kPCol + (uint32_t)(128 * h);
-                            const uint32_t idesc = idesc_tf32(Nh);
-                            const uint64_t boff = (uint64_t)(h * 128 * 128) >> 4;  // rows 128h.. of the B tiles
+        int t = blockIdx.x, l = 0, c = 0;
+        if (t < ntiles) {
+            load_b(p, b0, b_full, l, c, b_issued++);
+            if (chunk_after(p, ntiles, t, l, c, 1)) load_b(p, b0, b_full, l, c, b_issued++);
+        }
+    }
+
+    uint32_t j = 0, pu = 0;  // chunks seen consumed; partials of this group drained
+    bool ok = true;
+    float acc[128];
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        for (int l = 0; l < nl && ok; l++) {
+            const int nch = p.L[l].nch, Np = p.L[l].Np;
+            const bool has_half = 128 * g < Np;
 #pragma unroll
-                            for (int kq = 0; kq < 2; kq++) {
-                                const int kk = 2 * sub + kq;
-                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
-                                umma_tf32(d, al + adv, bh + boff + adv, idesc, kq);
-                                umma_tf32(d, ah + adv, bl + boff + adv, idesc, 1);
-                                umma_tf32(d, ah + adv, bh + boff + adv, idesc, 1);
+            for (int q = 0; q < 128; q++) acc[q] = 0.f;
+            if (a_owner(l, 0) == g) stage_a(p, a0, a_full, lane_base, r, t, l, 0, j);
+            if (nch > 1 && a_owner(l, 1) == g) stage_a(p, a0, a_full, lane_base, r, t, l, 1, j + 1);
+            for (int c = 0; c < nch && ok; c++) {
+                const uint32_t jj = j + (uint32_t)c;
+                const int s = jj & 1;
+                if (has_half) {
+                    uint64_t ah = 0, al = 0, bh = 0, bl = 0;
+                    uint32_t idesc = 0;
+                    if (issuer) {
+                        ok = mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, (l << 8) | c, (int)jj, g, 0) &&
+                             mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, (l << 8) | c, (int)jj, g, 0);
+                        tc_fence_after();
+                        ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
+                        al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
+                        const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;  // rows 128g.. of the B tiles
+                        bh = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile)) + boff;
+                        bl = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile + kBTile)) + boff;
+                        idesc = idesc_tf32(min(128, Np - 128 * g));
+                    }
+                    ok = __all_sync(0xffffffffu, ok);
+#pragma unroll 1
+                    for (int sub = 0; sub < 2 && ok; sub++) {
+                        if (issuer) {
+                            ok = mbar_wait(&p_empty[g], (pu & 1) ^ 1, p.err, 4, (l << 16) | (c << 8) | sub, (int)pu,
+                                           (int)jj, 0);
+                            if (ok) {
+                                tc_fence_after();
+                                const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
+#pragma unroll
+                                for (int kq = 0; kq < 2; kq++) {
+                                    const uint64_t adv = (uint64_t)(((2 * sub + kq) * 32) >> 4);  // 8 tf32 along K
+                                    umma_tf32(d, al + adv, bh + adv, idesc, kq);
+                                    umma_tf32(d, ah + adv, bl + adv, idesc, 1);
+                                    umma_tf32(d, ah + adv, bh + adv, idesc, 1);
+                                }
+                                umma_commit(&p_full[g]);
                             }
-                            umma_commit(&p_full[h]);
-                            pu[h]++;
                         }
+                        ok = __all_sync(0xffffffffu, ok);
+                        if (!ok) break;
+                        // the partial: add it into acc, four TMEM loads in flight
+                        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 16) | (c << 8) | sub,
+                                                               (int)pu, (int)jj, slot));
+                        if (!ok) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int q0 = 0; q0 < 8; q0 += 4) {
+                            if (128 * g + 16 * q0 < Np) {
+                                uint32_t v[4][16];
+#pragma unroll
+                                for (int u = 0; u < 4; u++)
+                                    if (128 * g + 16 * (q0 + u) < Np)
+                                        tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int u = 0; u < 4; u++)
+                                    if (128 * g + 16 * (q0 + u) < Np) {
+#pragma unroll
+                                        for (int e = 0; e < 16; e++) acc[16 * (q0 + u) + e] += __uint_as_float(v[u][e]);
+                                    }
+                            }
+                        }
+                        tc_fence_before();
+                        mbar_arrive(&p_empty[g]);
+                        pu++;
+                    }
                     if (!ok) break;
-                    umma_commit(&a_empty[sa]);
-                    umma_commit(&b_empty[sb]);
+                }
+                // this group is done with chunk jj (commit arrives once its MMAs completed)
+                if (issuer) umma_commit(&a_empty[s]);
+                // Every thread observes the consumption of every chunk in order, so every
+                // later wait on any ring barrier is at most one phase ahead: no aliasing.
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)pu, slot));
+                if (!ok) break;
+                if (c + 2 < nch && a_owner(l, c + 2) == g) stage_a(p, a0, a_full, lane_base, r, t, l, c + 2, jj + 2);
+                if (loader) {  // ring slot s is free: load the chunk two ahead
+                    b_done = jj + 1;
+                    int t2 = t, l2 = l, c2 = c;
+                    if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, b_issued++);
                 }
             }
-        // drain: every MMA issued above has completed before TMEM is freed
-        umma_commit(drain);
-        mbar_wait(drain, 0, p.err, 0);
-    } else if (warp >= 2) {
-        // ---------------- converters: group g owns output columns [128g, 128g+128) ----------------
-        const int g = (warp - 2) >> 2, quad = warp & 3;
-        const int r = quad * 32 + lane;  // sample row in the tile == TMEM lane
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-        const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;  // diagnostics of this group
-        uint32_t ia = 0, pu = 0;
-        bool ok = true;
-        float acc[128];
-        for (int t = blockIdx.x; t < (int)ntiles && ok; t += gridDim.x) {
-            for (int l = 0; l < nl && ok; l++) {
-                const int nch = p.L[l].nch;
-                const bool has_half = 128 * g < p.L[l].Np;
+            j += (uint32_t)nch;
+            if (!ok || !has_half) continue;
+            // bias + activation of this half; into T for the next layer, or out
+            const float *bias = sbias + l * kNMax + 128 * g;
+            const int N = p.L[l].N, act = p.L[l].act;
+            if (l + 1 < nl) {
 #pragma unroll
-                for (int q = 0; q < 128; q++) acc[q] = 0.f;
-                if (a_owner(l, 0) == g) stage_a(p, a0, lane_base, r, t, l, 0, ia);
-                if (nch > 1 && a_owner(l, 1) == g) stage_a(p, a0, lane_base, r, t, l, 1, ia + 1);
-                for (int c = 0; c < nch && ok; c++) {
-                    if (has_half) {
-#pragma unroll 1
-                        for (int sub = 0; sub < 2 && ok; sub++) {
-                            // one 16-deep partial of this half: add it into acc
-                            ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 16) | (c << 8) | sub,
-                                                                   (int)pu, (int)ia, slot));
-                            if (!ok) break;
-                            tc_fence_after();
-                            const int Np = p.L[l].Np;
+                for (int q = 0; q < 8; q++) {
+                    float v[16];
 #pragma unroll
-                            for (int q = 0; q < 8; q++) {
-                                if (128 * g + 16 * q < Np) {
-                                    float v[16];
-                                    tmem_ld16(lane_base + kPCol + (uint32_t)(128 * g + 16 * q), v);
-#pragma unroll
-                                    for (int e = 0; e < 16; e++) acc[16 * q + e] += v[e];
-                                }
-                            }
-                            tc_fence_before();
-                            mbar_arrive(&p_empty[g]);
-                            pu++;
-                        }
-                        if (!ok) break;
+                    for (int e = 0; e < 16; e++) {
+                        const int col = 128 * g + 16 * q + e;
+                        v[e] = col < N ? tc_act(acc[16 * q + e] + bias[16 * q + e], act) : 0.f;
                     }
-                    // Every converter thread observes the consumption of every A chunk in
-                    // order (whichever group staged it), so each a_empty phase is awaited by
-                    // a thread that has seen the previous one: the parity test cannot alias.
-                    const uint32_t j = ia + (uint32_t)c;
-                    ok = __all_sync(0xffffffffu,
-                                    mbar_wait(&a_empty[j & 1], (j >> 1) & 1, p.err, 5, (l << 8) | c, (int)j, (int)pu, slot));
-                    if (ok && c + 2 < nch && a_owner(l, c + 2) == g) stage_a(p, a0, lane_base, r, t, l, c + 2, j + 2);
+                    tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
                 }
-                ia += (uint32_t)nch;
-                if (!ok || !has_half) continue;
-                // bias + activation of this half; into T for the next layer, or out
-                const float *bias = sbias + l * kNMax + 128 * g;
-                const int N = p.L[l].N, act = p.L[l].act;
-                if (l + 1 < nl) {
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            } else {
+                const long long row0 = (long long)t * kBM + r;
+                if (row0 < p.n) {
+                    float *o = p.out + row0 + (long long)(128 * g) * p.ld_out;
 #pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        float v[16];
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            const int col = 128 * g + 16 * q + e;
-                            v[e] = col < N ? tc_act(acc[16 * q + e] + bias[16 * q + e], act) : 0.f;
-                        }
-                        tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
-                    }
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                } else {
-                    const long long row0 = (long long)t * kBM + r;
-                    if (row0 < p.n) {
-                        float *o = p.out + row0 + (long long)(128 * g) * p.ld_out;
-#pragma unroll
-                        for (int q = 0; q < 128; q++)
-                            if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act(acc[q] + bias[q], act);
-                    }
+                    for (int q = 0; q < 128; q++)
+                        if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act(acc[q] + bias[q], act);
                 }
             }
         }
     }
+    // Before TMEM and shared memory go away: the issuers' MMAs have completed
+    // (each group saw its last partial, every chunk's a_empty) and the loader's
+    // copies have landed.  On an error path, wait (bounded) for what is in flight.
+    if (issuer) {
+        umma_commit(&p_full[g]);  // an extra phase of p_full: completes when all this thread's MMAs are done
+        mbar_wait(&p_full[g], pu & 1, p.err, 0);
+    }
+    if (loader)  // chunks loaded but not seen consumed (only on an error path) must land first
+        for (uint32_t k = b_done; k < b_issued; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 0) {
         __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
