@@ -395,6 +395,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                                     umma_tf32(d, ah + adv, bh + adv, idesc, 1);
                                 }
                                 umma_commit(&p_full[g]);
+                                // after the chunk's last MMAs: the chunk is released when they
+                                // complete, not when this group has drained them
+                                if (sub == 1) umma_commit(&a_empty[s]);
                             }
                         }
                         ok = __all_sync(0xffffffffu, ok);
@@ -427,8 +430,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                     }
                     if (!ok) break;
                 }
-                // this group is done with chunk jj (commit arrives once its MMAs completed)
-                if (issuer) umma_commit(&a_empty[s]);
+                // a group without columns in this layer releases the chunk at once
+                if (issuer && !has_half) umma_commit(&a_empty[s]);
                 // Every thread observes the consumption of every chunk in order, so every
                 // later wait on any ring barrier is at most one phase ahead: no aliasing.
                 ok = __all_sync(0xffffffffu,
