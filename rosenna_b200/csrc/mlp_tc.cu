@@ -13,10 +13,10 @@
 // group owns sample row r (TMEM lane r):
 //   - one lane of each group issues that group's tcgen05.mma (M=128 samples,
 //     N=128 columns, K=8; three per K-step for the 3xTF32 split) into its own
-//     TMEM partial buffer, 16 K at a time; the group adds each partial into fp32
-//     registers (round-to-nearest: the tensor core truncates while it
-//     accumulates, so long chains inside TMEM lose accuracy).  While one group
-//     drains, the other group's MMAs run.
+//     TMEM partial buffer, one 32-deep partial per K-chunk with the small terms
+//     first; the group adds each partial into fp32 registers (round-to-nearest:
+//     the tensor core truncates while it accumulates, so long chains inside
+//     TMEM lose accuracy).  While one group drains, the other group's MMAs run.
 //   - one lane streams [Wh | Wl] K-chunks of 32 (128-byte swizzled rows) by TMA
 //     into a 2-stage ring, two chunks ahead of the MMAs.
 //   - the A operand of layer 0 is the input tile, of later layers the previous
@@ -379,33 +379,37 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                         idesc = idesc_tf32(min(128, Np - 128 * g));
                     }
                     ok = __all_sync(0xffffffffu, ok);
-#pragma unroll 1
-                    for (int sub = 0; sub < 2 && ok; sub++) {
-                        if (issuer) {
-                            ok = mbar_wait(&p_empty[g], (pu & 1) ^ 1, p.err, 4, (l << 16) | (c << 8) | sub, (int)pu,
-                                           (int)jj, 0);
-                            if (ok) {
-                                tc_fence_after();
-                                const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
+                    // One partial per chunk: the 32-deep product of this half, small
+                    // terms (Al*Wh, Ah*Wl) first, then Ah*Wh, so the truncating
+                    // accumulation adds the big terms to an accumulator that holds only
+                    // small ones.  The group sums the partials in fp32 registers.
+                    if (issuer) {
+                        ok = mbar_wait(&p_empty[g], (pu & 1) ^ 1, p.err, 4, (l << 8) | c, (int)pu, (int)jj, 0);
+                        if (ok) {
+                            tc_fence_after();
+                            const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
 #pragma unroll
-                                for (int kq = 0; kq < 2; kq++) {
-                                    const uint64_t adv = (uint64_t)(((2 * sub + kq) * 32) >> 4);  // 8 tf32 along K
-                                    umma_tf32(d, al + adv, bh + adv, idesc, kq);
-                                    umma_tf32(d, ah + adv, bl + adv, idesc, 1);
-                                    umma_tf32(d, ah + adv, bh + adv, idesc, 1);
-                                }
-                                umma_commit(&p_full[g]);
-                                // after the chunk's last MMAs: the chunk is released when they
-                                // complete, not when this group has drained them
-                                if (sub == 1) umma_commit(&a_empty[s]);
+                            for (int kk = 0; kk < kKC / 8; kk++) {
+                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
+                                umma_tf32(d, al + adv, bh + adv, idesc, kk);
+                                umma_tf32(d, ah + adv, bl + adv, idesc, 1);
                             }
+#pragma unroll
+                            for (int kk = 0; kk < kKC / 8; kk++) {
+                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+                                umma_tf32(d, ah + adv, bh + adv, idesc, 1);
+                            }
+                            umma_commit(&p_full[g]);
+                            umma_commit(&a_empty[s]);  // the chunk is released when these MMAs complete
                         }
-                        ok = __all_sync(0xffffffffu, ok);
-                        if (!ok) break;
+                    }
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (ok) {
                         // the partial: add it into acc, four TMEM loads in flight
-                        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 16) | (c << 8) | sub,
-                                                               (int)pu, (int)jj, slot));
-                        if (!ok) break;
+                        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 8) | c, (int)pu,
+                                                               (int)jj, slot));
+                    }
+                    if (ok) {
                         tc_fence_after();
 #pragma unroll
                         for (int q0 = 0; q0 < 8; q0 += 4) {
