@@ -16,13 +16,16 @@
 //     TMEM partial buffer, one 32-deep partial per K-chunk with the small terms
 //     first; the group adds each partial into fp32 registers (round-to-nearest:
 //     the tensor core truncates while it accumulates, so long chains inside
-//     TMEM lose accuracy).  While one group drains, the other group's MMAs run.
+//     TMEM lose accuracy).  A group issues the next chunk's MMAs as soon as it
+//     has drained the previous partial, before it stages anything.
 //   - one lane streams [Wh | Wl] K-chunks of 32 (128-byte swizzled rows) by TMA
 //     into a 2-stage ring, two chunks ahead of the MMAs.
 //   - the A operand of layer 0 is the input tile, of later layers the previous
-//     layer's activations (kept in TMEM), split hi/lo into a 2-stage smem ring.
+//     layer's activations (kept in TMEM); each group splits one 16-wide K half
+//     of every chunk into tf32 hi/lo in a 2-stage smem ring.
 //   - after the last K-chunk a group adds bias, applies the activation and
-//     writes its half to TMEM for the next layer, or to global memory.
+//     writes its half to TMEM for the next layer (handed over to the other
+//     group through an mbarrier), or to global memory.
 // Every wait on an mbarrier is bounded; on time-out the kernel records an error
 // code and where it waited in `err`, lets every role finish, frees TMEM and
 // returns.
@@ -203,13 +206,12 @@ __device__ __forceinline__ float tc_sigmoid(float x) {
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
     return r;
 }
-__device__ __forceinline__ float tc_act(float v, int act) {
-    switch (act) {
-        case 1: return v < 0.f ? 0.f : v;
-        case 2: return tc_tanh(v);
-        case 3: return tc_sigmoid(v);
-        default: return v;
-    }
+template <int ACT>
+__device__ __forceinline__ float tc_act(float v) {
+    if (ACT == 1) return v < 0.f ? 0.f : v;
+    if (ACT == 2) return tc_tanh(v);
+    if (ACT == 3) return tc_sigmoid(v);
+    return v;
 }
 
 // Writes 16 values (k = k0..k0+15 of this chunk) of row r into the hi/lo A
@@ -242,33 +244,28 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
         "r"(__float_as_uint(v[15])));
 }
 
-// Which converter group (column half) stages A chunk c of layer l: the input
-// layer alternates; hidden layers read chunk c from the half holding its columns.
-__device__ __forceinline__ int a_owner(int l, int c) { return l == 0 ? (c & 1) : (c >> 2); }
-
-// Stages A chunk c of layer l (tile t) into A ring slot j&1 for this thread's
-// row: the input layer from global memory, hidden layers from TMEM (the
-// previous layer's activations), split into tf32 hi/lo, 128-byte swizzled.
-// The slot is known free (chunk j-2 was seen consumed).
-__device__ __forceinline__ void stage_a(const TcArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base, int r,
-                                        int t, int l, int c, uint32_t j) {
+// Stages this group's K half (k = 16g..16g+15) of A chunk c of layer l (tile t)
+// into A ring slot j&1 for this thread's row: the input layer from global
+// memory, later layers from TMEM (the previous layer's activations), split into
+// tf32 hi/lo, 128-byte swizzled.  The slot is known free (chunk j-2 was seen
+// consumed); a_full completes when both groups have staged their halves.
+__device__ __forceinline__ void stage_half(const TcArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base, int r,
+                                           int g, int t, int l, int c, uint32_t j) {
     uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
-#pragma unroll 1
-    for (int h = 0; h < 2; h++) {
-        float v[16];
-        if (l == 0) {
-            const long long row = (long long)t * kBM + r;
-            const bool valid = row < p.n;
+    float v[16];
+    const int k0 = c * kKC + 16 * g;
+    if (l == 0) {
+        const long long row = (long long)t * kBM + r;
+        const bool valid = row < p.n;
 #pragma unroll
-            for (int e = 0; e < 16; e++) {
-                const int k = c * kKC + h * 16 + e;
-                v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + row) : 0.f;
-            }
-        } else {
-            tmem_ld16(lane_base + kTCol + (uint32_t)(c * kKC + h * 16), v);
+        for (int e = 0; e < 16; e++) {
+            const int k = k0 + e;
+            v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + row) : 0.f;
         }
-        put_a16(ahi, ahi + kATile, r, h * 16, v);
+    } else {
+        tmem_ld16(lane_base + kTCol + (uint32_t)k0, v);
     }
+    put_a16(ahi, ahi + kATile, r, 16 * g, v);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     mbar_arrive(&a_full[j & 1]);
@@ -295,6 +292,78 @@ __device__ __forceinline__ void load_b(const TcArgs &p, uint8_t *b0, uint64_t *b
     tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
 }
 
+// Issues the MMAs of this group's half for chunk jj (layer l, K-chunk c) as
+// partial number pi: waits for the B and A stages and for the group to have
+// drained the previous partial, then one 32-deep product with the small terms
+// (Al*Wh, Ah*Wl) first and Ah*Wh last, so the truncating accumulation adds the
+// big terms to an accumulator that holds only small ones.  Commits p_full (the
+// partial) and a_empty (this group's use of the A/B stage).
+__device__ __forceinline__ bool issue_chunk(const TcArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
+                                            uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full,
+                                            uint64_t *p_empty, uint32_t tmem, int g, int l, int c, uint32_t jj,
+                                            uint32_t pi) {
+    const int s = jj & 1;
+    const int where = (l << 8) | c;
+    if (!mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, where, (int)jj, g, 0)) return false;
+    if (!mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, where, (int)jj, g, 0)) return false;
+    if (!mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, where, (int)pi, (int)jj, 0)) return false;
+    tc_fence_after();
+    const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
+    const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
+    const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;  // rows 128g.. of the B tiles
+    const uint64_t bh = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile)) + boff;
+    const uint64_t bl = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile + kBTile)) + boff;
+    const uint32_t idesc = idesc_tf32(min(128, p.L[l].Np - 128 * g));
+    const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
+#pragma unroll
+    for (int kk = 0; kk < kKC / 8; kk++) {
+        const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
+        umma_tf32(d, al + adv, bh + adv, idesc, kk);
+        umma_tf32(d, ah + adv, bl + adv, idesc, 1);
+    }
+#pragma unroll
+    for (int kk = 0; kk < kKC / 8; kk++) {
+        const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+        umma_tf32(d, ah + adv, bh + adv, idesc, 1);
+    }
+    umma_commit(&p_full[g]);
+    umma_commit(&a_empty[s]);  // the stage is released when these MMAs complete
+    return true;
+}
+
+// Adds bias, applies the activation and writes this group's half of the layer
+// output: into TMEM T for the next layer, or to global memory.
+template <int ACT>
+__device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc)[128], const float *bias, int N, int g,
+                                              uint32_t lane_base, bool last, int t, int r) {
+    if (!last) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            float v[16];
+#pragma unroll
+            for (int e4 = 0; e4 < 4; e4++) {
+                const float4 b4 = reinterpret_cast<const float4 *>(bias)[4 * q + e4];
+                const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int i = 16 * q + 4 * e4 + e;
+                    const float y = tc_act<ACT>(acc[i] + bb[e]);
+                    v[4 * e4 + e] = 128 * g + i < N ? y : 0.f;
+                }
+            }
+            tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
+        }
+    } else {
+        const long long row0 = (long long)t * kBM + r;
+        if (row0 < p.n) {
+            float *o = p.out + row0 + (long long)(128 * g) * p.ld_out;
+#pragma unroll
+            for (int q = 0; q < 128; q++)
+                if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act<ACT>(acc[q] + bias[q]);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
@@ -303,8 +372,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     float *const sbias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
     uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
-    uint64_t *const p_full = bars + 6, *const p_empty = bars + 8;
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+    uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = warp >> 2, quad = warp & 3;
@@ -322,11 +391,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
-            mbar_init(&a_full[s], kBM);
-            mbar_init(&a_empty[s], 2);  // one tcgen05.commit per group
+            mbar_init(&a_full[s], kThreadsTc);  // both groups stage a K half
+            mbar_init(&a_empty[s], 2);          // one tcgen05.commit per group
             mbar_init(&p_full[s], 1);
             mbar_init(&p_empty[s], kBM);
         }
+        mbar_init(t_ready, kThreadsTc);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -350,7 +420,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         }
     }
 
-    uint32_t j = 0, pu = 0;  // chunks seen consumed; partials of this group drained
+    // j: chunks seen consumed; pu / pi: partials of this group drained / issued;
+    // tb: T hand-overs between layers seen
+    uint32_t j = 0, pu = 0, pi = 0, tb = 0;
     bool ok = true;
     float acc[128];
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -359,129 +431,96 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             const bool has_half = 128 * g < Np;
 #pragma unroll
             for (int q = 0; q < 128; q++) acc[q] = 0.f;
-            if (a_owner(l, 0) == g) stage_a(p, a0, a_full, lane_base, r, t, l, 0, j);
-            if (nch > 1 && a_owner(l, 1) == g) stage_a(p, a0, a_full, lane_base, r, t, l, 1, j + 1);
+            stage_half(p, a0, a_full, lane_base, r, g, t, l, 0, j);
+            if (nch > 1) stage_half(p, a0, a_full, lane_base, r, g, t, l, 1, j + 1);
+            if (has_half && issuer) {
+                ok = issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, 0, j, pi);
+                pi += ok;
+            }
+            ok = __all_sync(0xffffffffu, ok);
             for (int c = 0; c < nch && ok; c++) {
                 const uint32_t jj = j + (uint32_t)c;
                 const int s = jj & 1;
                 if (has_half) {
-                    uint64_t ah = 0, al = 0, bh = 0, bl = 0;
-                    uint32_t idesc = 0;
-                    if (issuer) {
-                        ok = mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, (l << 8) | c, (int)jj, g, 0) &&
-                             mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, (l << 8) | c, (int)jj, g, 0);
-                        tc_fence_after();
-                        ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
-                        al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
-                        const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;  // rows 128g.. of the B tiles
-                        bh = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile)) + boff;
-                        bl = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile + kBTile)) + boff;
-                        idesc = idesc_tf32(min(128, Np - 128 * g));
-                    }
-                    ok = __all_sync(0xffffffffu, ok);
-                    // One partial per chunk: the 32-deep product of this half, small
-                    // terms (Al*Wh, Ah*Wl) first, then Ah*Wh, so the truncating
-                    // accumulation adds the big terms to an accumulator that holds only
-                    // small ones.  The group sums the partials in fp32 registers.
-                    if (issuer) {
-                        ok = mbar_wait(&p_empty[g], (pu & 1) ^ 1, p.err, 4, (l << 8) | c, (int)pu, (int)jj, 0);
-                        if (ok) {
-                            tc_fence_after();
-                            const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
-#pragma unroll
-                            for (int kk = 0; kk < kKC / 8; kk++) {
-                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
-                                umma_tf32(d, al + adv, bh + adv, idesc, kk);
-                                umma_tf32(d, ah + adv, bl + adv, idesc, 1);
-                            }
-#pragma unroll
-                            for (int kk = 0; kk < kKC / 8; kk++) {
-                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);
-                                umma_tf32(d, ah + adv, bh + adv, idesc, 1);
-                            }
-                            umma_commit(&p_full[g]);
-                            umma_commit(&a_empty[s]);  // the chunk is released when these MMAs complete
-                        }
-                    }
-                    ok = __all_sync(0xffffffffu, ok);
-                    if (ok) {
-                        // the partial: add it into acc, four TMEM loads in flight
-                        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 8) | c, (int)pu,
-                                                               (int)jj, slot));
-                    }
-                    if (ok) {
-                        tc_fence_after();
-#pragma unroll
-                        for (int q0 = 0; q0 < 8; q0 += 4) {
-                            if (128 * g + 16 * q0 < Np) {
-                                uint32_t v[4][16];
-#pragma unroll
-                                for (int u = 0; u < 4; u++)
-                                    if (128 * g + 16 * (q0 + u) < Np)
-                                        tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
-                                tmem_wait_ld();
-#pragma unroll
-                                for (int u = 0; u < 4; u++)
-                                    if (128 * g + 16 * (q0 + u) < Np) {
-#pragma unroll
-                                        for (int e = 0; e < 16; e++) acc[16 * (q0 + u) + e] += __uint_as_float(v[u][e]);
-                                    }
-                            }
-                        }
-                        tc_fence_before();
-                        mbar_arrive(&p_empty[g]);
-                        pu++;
-                    }
+                    // partial of chunk c: add it into acc, four TMEM loads in flight
+                    ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 8) | c, (int)pu,
+                                                           (int)jj, slot));
                     if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int q0 = 0; q0 < 8; q0 += 4) {
+                        if (128 * g + 16 * q0 < Np) {
+                            uint32_t v[4][16];
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (128 * g + 16 * (q0 + u) < Np)
+                                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (128 * g + 16 * (q0 + u) < Np) {
+#pragma unroll
+                                    for (int e = 0; e < 16; e++) acc[16 * (q0 + u) + e] += __uint_as_float(v[u][e]);
+                                }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&p_empty[g]);
+                    pu++;
+                    // the next chunk's MMAs go in before this thread stages anything
+                    if (issuer && c + 1 < nch) {
+                        ok = issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, c + 1,
+                                         jj + 1, pi);
+                        pi += ok;
+                    }
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) break;
+                } else if (issuer) {
+                    umma_commit(&a_empty[s]);  // a group without columns in this layer releases the stage at once
                 }
-                // a group without columns in this layer releases the chunk at once
-                if (issuer && !has_half) umma_commit(&a_empty[s]);
                 // Every thread observes the consumption of every chunk in order, so every
                 // later wait on any ring barrier is at most one phase ahead: no aliasing.
                 ok = __all_sync(0xffffffffu,
                                 mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)pu, slot));
                 if (!ok) break;
-                if (c + 2 < nch && a_owner(l, c + 2) == g) stage_a(p, a0, a_full, lane_base, r, t, l, c + 2, jj + 2);
-                if (loader) {  // ring slot s is free: load the chunk two ahead
+                if (c + 2 < nch) stage_half(p, a0, a_full, lane_base, r, g, t, l, c + 2, jj + 2);
+                if (loader) {  // ring stage s is free: load the chunk two ahead
                     b_done = jj + 1;
                     int t2 = t, l2 = l, c2 = c;
                     if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, b_issued++);
                 }
             }
             j += (uint32_t)nch;
-            if (!ok || !has_half) continue;
-            // bias + activation of this half; into T for the next layer, or out
-            const float *bias = sbias + l * kNMax + 128 * g;
-            const int N = p.L[l].N, act = p.L[l].act;
-            if (l + 1 < nl) {
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    float v[16];
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const int col = 128 * g + 16 * q + e;
-                        v[e] = col < N ? tc_act(acc[16 * q + e] + bias[16 * q + e], act) : 0.f;
-                    }
-                    tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
+            if (!ok) break;
+            const bool last = l + 1 == nl;
+            if (has_half) {
+                const float *bias = sbias + l * kNMax + 128 * g;
+                switch (p.L[l].act) {
+                    case 1: finalize_half<1>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
+                    case 2: finalize_half<2>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
+                    case 3: finalize_half<3>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
+                    default: finalize_half<0>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
                 }
+            }
+            if (!last) {
+                // the next layer stages K halves that the other group wrote: hand T over
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            } else {
-                const long long row0 = (long long)t * kBM + r;
-                if (row0 < p.n) {
-                    float *o = p.out + row0 + (long long)(128 * g) * p.ld_out;
-#pragma unroll
-                    for (int q = 0; q < 128; q++)
-                        if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act(acc[q] + bias[q], act);
-                }
+                tc_fence_before();
+                mbar_arrive(t_ready);
+                ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, l, (int)tb, (int)j, slot));
+                tb++;
+                tc_fence_after();
             }
         }
     }
     // Before TMEM and shared memory go away: the issuers' MMAs have completed
     // (each group saw its last partial, every chunk's a_empty) and the loader's
-    // copies have landed.  On an error path, wait (bounded) for what is in flight.
+    // copies have landed.  On an error path, wait (bounded) for what is in flight:
+    // an extra commit on p_full completes when all of this thread's MMAs are done,
+    // its phases are waited in order.
     if (issuer) {
-        umma_commit(&p_full[g]);  // an extra phase of p_full: completes when all this thread's MMAs are done
-        mbar_wait(&p_full[g], pu & 1, p.err, 0);
+        umma_commit(&p_full[g]);
+        for (uint32_t k = pu; k <= pi; k++) mbar_wait(&p_full[g], k & 1, p.err, 0);
     }
     if (loader)  // chunks loaded but not seen consumed (only on an error path) must land first
         for (uint32_t k = b_done; k < b_issued; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
