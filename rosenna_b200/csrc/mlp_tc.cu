@@ -11,18 +11,21 @@
 // Per CTA (one per SM, persistent over tiles of 128 samples), 8 warps in two
 // groups of four; group g owns output columns [128g, 128g+128) and thread r of a
 // group owns sample row r (TMEM lane r):
-//   - one lane of each group issues that group's tcgen05.mma (M=128 samples,
-//     N=128 columns, K=8; three per K-step for the 3xTF32 split) into its own
-//     TMEM partial buffer, one 32-deep partial per K-chunk with the small terms
-//     first; the group adds each partial into fp32 registers (round-to-nearest:
-//     the tensor core truncates while it accumulates, so long chains inside
-//     TMEM lose accuracy).  A group issues the next chunk's MMAs as soon as it
-//     has drained the previous partial, before it stages anything.
+//   - one lane of each group (warps 0 and 5) issues that group's tcgen05.mma
+//     (M=128 samples, N=128 columns, K=8; three per K-step for the 3xTF32
+//     split) into its own TMEM partial buffer, one 32-deep partial per K-chunk
+//     with the small terms first; the group adds each partial into fp32
+//     registers (round-to-nearest: the tensor core truncates while it
+//     accumulates, so long chains inside TMEM lose accuracy).  A group issues
+//     the next chunk's MMAs as soon as it has drained the previous partial; the
+//     halves take turns in the tensor pipe, so one drains while the other
+//     computes.  Issuing holds the issuing warp until its MMAs are nearly done,
+//     so the issuers' warps stage nothing.
 //   - one lane streams [Wh | Wl] K-chunks of 32 (128-byte swizzled rows) by TMA
 //     into a 2-stage ring, two chunks ahead of the MMAs.
 //   - the A operand of layer 0 is the input tile, of later layers the previous
-//     layer's activations (kept in TMEM); each group splits one 16-wide K half
-//     of every chunk into tf32 hi/lo in a 2-stage smem ring.
+//     layer's activations (kept in TMEM), split into tf32 hi/lo in a 2-stage
+//     smem ring by the six staging warps (16-wide K halves of each chunk).
 //   - after the last K-chunk a group adds bias, applies the activation and
 //     writes its half to TMEM for the next layer (handed over to the other
 //     group through an mbarrier), or to global memory.
@@ -43,6 +46,7 @@ constexpr int kBM = 128;                 // samples per tile (UMMA M)
 constexpr int kKC = 32;                  // K per chunk: 32 fp32 = one 128-byte swizzle row
 constexpr int kNMax = 256;               // widest layer (UMMA N)
 constexpr int kThreadsTc = 256;           // two groups of four warps (2 warps per SMSP: up to 255 registers)
+constexpr int kStagers = 6 * 32;          // threads that stage A (all but the issuers' warps)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTCol = 0;             // TMEM cols [0,256): previous layer's activations
 constexpr uint32_t kPCol = 256;           // TMEM cols [256,512): partial sums of column half h at 256+128h
@@ -244,28 +248,33 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
         "r"(__float_as_uint(v[15])));
 }
 
-// Stages this group's K half (k = 16g..16g+15) of A chunk c of layer l (tile t)
-// into A ring slot j&1 for this thread's row: the input layer from global
-// memory, later layers from TMEM (the previous layer's activations), split into
-// tf32 hi/lo, 128-byte swizzled.  The slot is known free (chunk j-2 was seen
-// consumed); a_full completes when both groups have staged their halves.
-__device__ __forceinline__ void stage_half(const TcArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base, int r,
-                                           int g, int t, int l, int c, uint32_t j) {
+// Stages the K halves in `halves` (bit h: k = 16h..16h+15) of A chunk c of
+// layer l (tile t) into A ring slot j&1 for this thread's row: the input layer
+// from global memory, later layers from TMEM (the previous layer's
+// activations), split into tf32 hi/lo, 128-byte swizzled.  The slot is known
+// free (chunk j-2 was seen consumed); a_full completes when every staging
+// thread has arrived.
+__device__ __forceinline__ void stage_halves(const TcArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base, int r,
+                                             int halves, int t, int l, int c, uint32_t j) {
     uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
-    float v[16];
-    const int k0 = c * kKC + 16 * g;
-    if (l == 0) {
-        const long long row = (long long)t * kBM + r;
-        const bool valid = row < p.n;
+#pragma unroll 1
+    for (int h = 0; h < 2; h++) {
+        if (!(halves & (1 << h))) continue;
+        float v[16];
+        const int k0 = c * kKC + 16 * h;
+        if (l == 0) {
+            const long long row = (long long)t * kBM + r;
+            const bool valid = row < p.n;
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-            const int k = k0 + e;
-            v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + row) : 0.f;
+            for (int e = 0; e < 16; e++) {
+                const int k = k0 + e;
+                v[e] = (valid && k < p.L[0].K) ? __ldg(p.in + (long long)k * p.ld_in + row) : 0.f;
+            }
+        } else {
+            tmem_ld16(lane_base + kTCol + (uint32_t)k0, v);
         }
-    } else {
-        tmem_ld16(lane_base + kTCol + (uint32_t)k0, v);
+        put_a16(ahi, ahi + kATile, r, 16 * h, v);
     }
-    put_a16(ahi, ahi + kATile, r, 16 * g, v);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     mbar_arrive(&a_full[j & 1]);
@@ -331,6 +340,23 @@ __device__ __forceinline__ bool issue_chunk(const TcArgs &p, uint8_t *a0, uint8_
     return true;
 }
 
+// issue_chunk in the halves' turn order: where both halves have columns, group
+// 1 issues chunk jj only after group 0 has issued it, so the two halves' MMAs
+// alternate in the tensor pipe and one half drains while the other computes.
+__device__ __forceinline__ bool issue_in_turn(const TcArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
+                                              uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full,
+                                              uint64_t *p_empty, uint64_t *turn, uint32_t tmem, int g, int l, int c,
+                                              uint32_t jj, uint32_t &pi, uint32_t &ts, bool both) {
+    if (g == 1 && both) {
+        if (!mbar_wait(turn, ts & 1, p.err, 8, (l << 8) | c, (int)ts, (int)jj, 0)) return false;
+        ts++;
+    }
+    if (!issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, c, jj, pi)) return false;
+    pi++;
+    if (g == 0 && both) mbar_arrive(turn);
+    return true;
+}
+
 // Adds bias, applies the activation and writes this group's half of the layer
 // output: into TMEM T for the next layer, or to global memory.
 template <int ACT>
@@ -373,13 +399,19 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
     uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+    uint64_t *const turn = bars + 11;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = warp >> 2, quad = warp & 3;
     const int r = quad * 32 + lane;                    // sample row in the tile == TMEM lane
-    const bool issuer = lane == 0 && quad == 0;        // issues this group's MMAs
-    const bool loader = g == 0 && lane == 0 && quad == 1;  // issues the TMA loads
+    // Issuing MMAs holds a thread until they are nearly done (the tensor pipe
+    // queues few), so the issuers' warps (0 and 5) stage nothing: warps 4 and 1
+    // stage both K halves of TMEM lane quadrants 0 and 1, the other warps their
+    // group's half.
+    const bool issuer = lane == 0 && (warp == 0 || warp == 5);  // issues this group's MMAs
+    const int halves = (warp == 0 || warp == 5) ? 0 : (warp == 1 || warp == 4) ? 3 : 1 << g;
+    const bool loader = warp == 2 && lane == 0;                 // issues the TMA loads
     const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;  // records this group's position on error
     const int nl = p.nlayers;
     const int ntiles = (int)((p.n + kBM - 1) / kBM);
@@ -391,12 +423,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
-            mbar_init(&a_full[s], kThreadsTc);  // both groups stage a K half
+            mbar_init(&a_full[s], kStagers);
             mbar_init(&a_empty[s], 2);          // one tcgen05.commit per group
             mbar_init(&p_full[s], 1);
             mbar_init(&p_empty[s], kBM);
         }
         mbar_init(t_ready, kThreadsTc);
+        mbar_init(turn, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -422,7 +455,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
 
     // j: chunks seen consumed; pu / pi: partials of this group drained / issued;
     // tb: T hand-overs between layers seen
-    uint32_t j = 0, pu = 0, pi = 0, tb = 0;
+    // ts: chunks of group 0 seen issued (group 1's issuer)
+    uint32_t j = 0, pu = 0, pi = 0, tb = 0, ts = 0;
     bool ok = true;
     float acc[128];
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -431,12 +465,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             const bool has_half = 128 * g < Np;
 #pragma unroll
             for (int q = 0; q < 128; q++) acc[q] = 0.f;
-            stage_half(p, a0, a_full, lane_base, r, g, t, l, 0, j);
-            if (nch > 1) stage_half(p, a0, a_full, lane_base, r, g, t, l, 1, j + 1);
-            if (has_half && issuer) {
-                ok = issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, 0, j, pi);
-                pi += ok;
+            const bool both = Np > 128;  // the halves take turns in the tensor pipe
+            if (halves) {
+                stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 0, j);
+                if (nch > 1) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 1, j + 1);
             }
+            if (has_half && issuer)
+                ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi,
+                                   ts, both);
             ok = __all_sync(0xffffffffu, ok);
             for (int c = 0; c < nch && ok; c++) {
                 const uint32_t jj = j + (uint32_t)c;
@@ -468,11 +504,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                     mbar_arrive(&p_empty[g]);
                     pu++;
                     // the next chunk's MMAs go in before this thread stages anything
-                    if (issuer && c + 1 < nch) {
-                        ok = issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, c + 1,
-                                         jj + 1, pi);
-                        pi += ok;
-                    }
+                    if (issuer && c + 1 < nch)
+                        ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l,
+                                           c + 1, jj + 1, pi, ts, both);
                     ok = __all_sync(0xffffffffu, ok);
                     if (!ok) break;
                 } else if (issuer) {
@@ -483,12 +517,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                 ok = __all_sync(0xffffffffu,
                                 mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)pu, slot));
                 if (!ok) break;
-                if (c + 2 < nch) stage_half(p, a0, a_full, lane_base, r, g, t, l, c + 2, jj + 2);
                 if (loader) {  // ring stage s is free: load the chunk two ahead
                     b_done = jj + 1;
                     int t2 = t, l2 = l, c2 = c;
                     if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, b_issued++);
                 }
+                if (c + 2 < nch && halves) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, c + 2, jj + 2);
             }
             j += (uint32_t)nch;
             if (!ok) break;
