@@ -55,6 +55,8 @@ constexpr uint32_t kATile = kBM * 128;    // bytes of one A tile (hi or lo)
 constexpr uint32_t kSmemB = 2 * 2 * kBTile;  // 2 stages x (hi, lo)
 constexpr uint32_t kSmemA = 2 * 2 * kATile;
 constexpr uint32_t kSmemBias = kTcMaxLayers * kNMax * 4;
+constexpr uint32_t kSmemTailW = kNMax * kTcTailMaxN * 4;  // tail W^T, rows of 16
+constexpr uint32_t kSmemX = kTcTailMaxN * kBM * 4;          // tail K-half exchange [n][row]
 constexpr uint32_t kSmemBars = 256;
 constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s
 constexpr uint32_t kWaitIters = 1u << 26;
@@ -245,7 +247,8 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
         "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
         "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
         "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-        "r"(__float_as_uint(v[15])));
+        "r"(__float_as_uint(v[15]))
+        : "memory");
 }
 
 // Stages the K halves in `halves` (bit h: k = 16h..16h+15) of A chunk c of
@@ -358,7 +361,10 @@ __device__ __forceinline__ bool issue_in_turn(const TcArgs &p, uint8_t *a0, uint
 }
 
 // Adds bias, applies the activation and writes this group's half of the layer
-// output: into TMEM T for the next layer, or to global memory.
+// output: into TMEM T for the next layer, or to global memory.  Columns at and
+// beyond N hold act(0) (their weight rows and bias are zero padding) and meet
+// zero weight columns in the next layer, so they need no masking.  The code is
+// kept short: it runs once per layer and is fetched cold each time.
 template <int ACT>
 __device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc)[128], const float *bias, int N, int g,
                                               uint32_t lane_base, bool last, int t, int r) {
@@ -384,10 +390,84 @@ __device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc
         if (row0 < p.n) {
             float *o = p.out + row0 + (long long)(128 * g) * p.ld_out;
 #pragma unroll
-            for (int q = 0; q < 128; q++)
-                if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act<ACT>(acc[q] + bias[q]);
+            for (int q0 = 0; q0 < 128; q0 += 16)
+                if (128 * g + q0 < N) {
+#pragma unroll
+                    for (int q = q0; q < q0 + 16; q++)
+                        if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act<ACT>(acc[q] + bias[q]);
+                }
         }
     }
+}
+
+// The last layer on the CUDA cores (fp32 FMA), for a narrow output (N <= 16)
+// whose MMA chunks would be latency-bound: each thread takes the dot products
+// of its row over its group's K half (its own T columns, below np_prev), group
+// 1 hands its partial sums to group 0 through shared memory, and group 0 adds
+// bias, applies the activation and writes the row.
+template <int NP>
+__device__ __noinline__ bool run_tail(const TcArgs &p, uint8_t *base, uint32_t lane_base, int g, int r, int t,
+                                      int np_prev, uint32_t &xt, int slot) {
+    const float *stail = reinterpret_cast<const float *>(base + kSmemB + kSmemA + kSmemBias);
+    float *sx = reinterpret_cast<float *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW);
+    const float *btail = reinterpret_cast<const float *>(base + kSmemB + kSmemA) + p.nlayers * kNMax;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
+    uint64_t *x_full = bars + 12, *x_empty = bars + 13;
+    float o[NP];
+#pragma unroll
+    for (int n = 0; n < NP; n++) o[n] = 0.f;
+#pragma unroll 1
+    for (int q = 0; q < 8; q++) {
+        const int k0 = 128 * g + 16 * q;
+        if (k0 >= np_prev) break;
+        float v[16];
+        tmem_ld16(lane_base + kTCol + (uint32_t)k0, v);
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            const float4 *w = reinterpret_cast<const float4 *>(stail + (k0 + e) * kTcTailMaxN);
+#pragma unroll
+            for (int n4 = 0; n4 < NP / 4; n4++) {
+                const float4 w4 = w[n4];
+                o[4 * n4 + 0] = fmaf(v[e], w4.x, o[4 * n4 + 0]);
+                o[4 * n4 + 1] = fmaf(v[e], w4.y, o[4 * n4 + 1]);
+                o[4 * n4 + 2] = fmaf(v[e], w4.z, o[4 * n4 + 2]);
+                o[4 * n4 + 3] = fmaf(v[e], w4.w, o[4 * n4 + 3]);
+            }
+        }
+    }
+    if (p.tail_k > 128) {  // both groups hold K columns: combine the halves
+        if (g == 1) {
+            if (!mbar_wait(x_empty, (xt & 1) ^ 1, p.err, 10, t, (int)xt, 0, slot)) return false;
+#pragma unroll
+            for (int n = 0; n < NP; n++) sx[n * kBM + r] = o[n];
+            mbar_arrive(x_full);
+        } else {
+            if (!mbar_wait(x_full, xt & 1, p.err, 11, t, (int)xt, 0, slot)) return false;
+#pragma unroll
+            for (int n = 0; n < NP; n++) o[n] += sx[n * kBM + r];
+            mbar_arrive(x_empty);
+        }
+        xt++;
+    }
+    if (g == 0) {
+        const long long row = (long long)t * kBM + r;
+        if (row < p.n) {
+#pragma unroll
+            for (int n = 0; n < NP; n++) {
+                if (n >= p.tail_n) break;
+                const float y = o[n] + btail[n];
+                float z;
+                switch (p.tail_act) {
+                    case 1: z = tc_act<1>(y); break;
+                    case 2: z = tc_act<2>(y); break;
+                    case 3: z = tc_act<3>(y); break;
+                    default: z = y; break;
+                }
+                p.out[row + (long long)n * p.ld_out] = z;
+            }
+        }
+    }
+    return true;
 }
 
 __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
@@ -396,11 +476,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     uint8_t *const b0 = base;           // B stage s: hi at b0 + s*2*kBTile, lo + kBTile
     uint8_t *const a0 = base + kSmemB;  // A stage s: hi at a0 + s*2*kATile, lo + kATile
     float *const sbias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
-    uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
     uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
     uint64_t *const turn = bars + 11;
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = warp >> 2, quad = warp & 3;
@@ -420,6 +500,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         const int l = i / kNMax, j = i - l * kNMax;
         sbias[i] = j < p.L[l].Np ? p.arena[p.L[l].b_off + j] : 0.f;
     }
+    if (p.tail_n > 0) {  // zero beyond K and tail_np: those activations meet zero weights
+        float *stail = reinterpret_cast<float *>(base + kSmemB + kSmemA + kSmemBias);
+        for (int i = tid; i < kNMax * kTcTailMaxN; i += kThreadsTc) {
+            const int k = i / kTcTailMaxN, n = i - k * kTcTailMaxN;
+            stail[i] = (k < p.tail_kp && n < p.tail_np) ? p.arena[p.tail_w_off + (long long)k * p.tail_np + n] : 0.f;
+        }
+        for (int i = tid; i < kTcTailMaxN; i += kThreadsTc)
+            sbias[nl * kNMax + i] = i < p.tail_np ? p.arena[p.tail_b_off + i] : 0.f;
+    }
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
@@ -430,6 +519,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         }
         mbar_init(t_ready, kThreadsTc);
         mbar_init(turn, 1);
+        mbar_init(bars + 12, kBM);  // tail exchange: full, empty
+        mbar_init(bars + 13, kBM);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -456,7 +547,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     // j: chunks seen consumed; pu / pi: partials of this group drained / issued;
     // tb: T hand-overs between layers seen
     // ts: chunks of group 0 seen issued (group 1's issuer)
-    uint32_t j = 0, pu = 0, pi = 0, tb = 0, ts = 0;
+    // xt: tail exchanges seen
+    uint32_t j = 0, pu = 0, pi = 0, tb = 0, ts = 0, xt = 0;
     bool ok = true;
     float acc[128];
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -527,14 +619,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             j += (uint32_t)nch;
             if (!ok) break;
             const bool last = l + 1 == nl;
+            const bool to_out = last && p.tail_n == 0;  // else T, for the next layer or the tail
             if (has_half) {
                 const float *bias = sbias + l * kNMax + 128 * g;
                 switch (p.L[l].act) {
-                    case 1: finalize_half<1>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
-                    case 2: finalize_half<2>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
-                    case 3: finalize_half<3>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
-                    default: finalize_half<0>(p, acc, bias, p.L[l].N, g, lane_base, last, t, r); break;
+                    case 1: finalize_half<1>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    case 2: finalize_half<2>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    case 3: finalize_half<3>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    default: finalize_half<0>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
                 }
+            }
+            if (last && !to_out) {
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                ok = p.tail_np == 8 ? run_tail<8>(p, base, lane_base, g, r, t, has_half ? Np : 0, xt, slot)
+                                    : run_tail<16>(p, base, lane_base, g, r, t, has_half ? Np : 0, xt, slot);
             }
             if (!last) {
                 // the next layer stages K halves that the other group wrote: hand T over
@@ -569,7 +668,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
 
 }  // namespace
 
-size_t mlp_tc_smem_bytes() { return 1024 + kSmemB + kSmemA + kSmemBias + kSmemBars; }
+size_t mlp_tc_smem_bytes() { return 1024 + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX + kSmemBars; }
 
 cudaError_t mlp_tc_configure() {
     return cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());

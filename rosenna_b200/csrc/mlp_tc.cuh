@@ -9,6 +9,7 @@
 namespace rosenna {
 
 constexpr int kTcMaxLayers = 8;
+constexpr int kTcTailMaxN = 16;  // widest last layer run as the CUDA-core tail
 
 // One layer; its packed weights are a [2*Np][Kp] fp32 block (rows 0..Np-1 the
 // tf32-rounded high parts W_hi[n][k], rows Np..2Np-1 the rounded remainders).
@@ -26,8 +27,13 @@ struct TcArgs {
     long long ld_out;
     long long n;
     int *err;  // [64]: err[0] = non-zero code when a wait times out, err[1..6] where, err[8r..] per role
-    int nlayers;
+    int nlayers;  // layers on the tensor cores
     TcLayer L[kTcMaxLayers];
+    // A narrow last layer (N <= 16) runs on the CUDA cores after them when
+    // tail_n > 0: fp32 W^T [tail_kp][tail_np] at arena offset tail_w_off (the
+    // FFMA kernel's layout), bias [tail_np] at tail_b_off.
+    int tail_n, tail_np, tail_k, tail_kp, tail_act;
+    long long tail_w_off, tail_b_off;
 };
 
 size_t mlp_tc_smem_bytes();

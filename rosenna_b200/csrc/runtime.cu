@@ -449,6 +449,20 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             a.arena = d->arena;
             a.err = d->err;
             a.nlayers = (int)s.layers.size();
+            // a narrow last layer runs on the CUDA cores at the end of the kernel
+            // (ROSENNA_TC_TAIL=0 keeps it on the tensor cores)
+            const MlpLayer &lastl = s.layers.back();
+            const char *tail_env = getenv("ROSENNA_TC_TAIL");
+            if (a.nlayers >= 2 && lastl.M <= kTcTailMaxN && !(tail_env && std::string(tail_env) == "0")) {
+                a.nlayers--;
+                a.tail_n = lastl.M;
+                a.tail_np = lastl.Mp;
+                a.tail_k = lastl.K;
+                a.tail_kp = lastl.Kp;
+                a.tail_act = lastl.act;
+                a.tail_w_off = lastl.w_off;
+                a.tail_b_off = lastl.b_off;
+            }
             for (int l = 0; l < a.nlayers; l++) {
                 const MlpLayer &ly = s.layers[(size_t)l];
                 a.L[l] = TcLayer{ly.K, ly.M, ly.tc_Kp, ly.tc_Np, ly.tc_Kp / 32, ly.act, ly.tc_w_off, ly.tc_b_off};

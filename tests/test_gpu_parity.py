@@ -130,15 +130,18 @@ def test_multi_gpu_split_matches(tmp_path):
     assert_close(out, ref.reshape(out.shape), "lstm multi-gpu")
 
 
-@pytest.mark.parametrize("path", ["tc", "ffma"])
+@pytest.mark.parametrize("path", ["tc", "tc_notail", "ffma"])
 @pytest.mark.parametrize("name", ["small_mlp", "wide_mlp", "cnn"])
 def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
-    """Both MLP kernels (tcgen05 3xTF32 and FFMA) on every MLP chain shape."""
-    monkeypatch.setenv("ROSENNA_MLP_PATH", path)
+    """Both MLP kernels (tcgen05 3xTF32 and FFMA) on every MLP chain shape; the
+    tensor-core kernel with its narrow last layer on the CUDA cores (default)
+    and on the tensor cores."""
+    monkeypatch.setenv("ROSENNA_MLP_PATH", "ffma" if path == "ffma" else "tc")
+    monkeypatch.setenv("ROSENNA_TC_TAIL", "0" if path == "tc_notail" else "1")
     workloads.write_model(name, str(tmp_path))
     api.initialize(str(tmp_path))
     desc = api.plan_description()
-    assert ("mlp_tc" in desc) == (path == "tc"), desc
+    assert ("mlp_tc" in desc) == (path != "ffma"), desc
     for n in (129, 4099):
         ins = workloads.make_inputs(name, n, seed_offset=7 + n)
         out = api.use_model_rows(ins)[0]
@@ -146,9 +149,11 @@ def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
         assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
 
 
+@pytest.mark.parametrize("tail", ["1", "0"])
 @pytest.mark.parametrize("case", ["gemm_small", "gemm_big", "batchnet", "droplet", "lstm_gemm_hid"])
-def test_golden_mlps_on_tensor_cores(case, monkeypatch):
+def test_golden_mlps_on_tensor_cores(case, tail, monkeypatch):
     monkeypatch.setenv("ROSENNA_MLP_PATH", "tc")
+    monkeypatch.setenv("ROSENNA_TC_TAIL", tail)
     d = goldens.case_dir(case)
     api.initialize(d)
     assert "mlp_tc" in api.plan_description()
