@@ -21,6 +21,7 @@ import argparse
 import json
 import os
 import statistics
+import threading
 import subprocess
 import sys
 import tempfile
@@ -78,53 +79,73 @@ def cpu_baseline(name, model_dir, target_seconds=12.0, steps=1):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons, polled through NVML every
+    10 ms on a background thread during the timed region (plus one sample at
+    each end), so that even a timed region of a few ms has samples."""
 
-    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, dev):
         self.dev = dev
-        self.proc = None
+        self.samples = []
+        self.stop = threading.Event()
+        self.nvml = None
+        self.handle = None
+
+    def _open(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            try:
+                import torch
+                pr = torch.cuda.get_device_properties(self.dev)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+        except Exception:
+            self.nvml = self.handle = None
+
+    def _sample(self):
+        n, h = self.nvml, self.handle
+        try:
+            sm = n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)
+            mx = n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM)
+            try:
+                r = n.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except AttributeError:
+                r = n.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+            self.samples.append((sm, mx, r))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self.stop.wait(0.01):
+            self._sample()
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.dev), "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        self._open()
+        if self.handle is not None:
+            self._sample()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
         return self
 
     def __exit__(self, *a):
-        self.out = ""
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out = ""
+        if self.handle is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            self._sample()
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (self.out or "").splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 7:
-                continue
-            try:
-                sm.append(float(f[0]))
-                mx.append(float(f[1]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[3:7]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": "nvml unavailable"}
+        reasons = sorted(k for k, bit in self.REASONS.items() if any(r & bit for _, _, r in self.samples))
+        return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons,
+                "samples": len(self.samples), "source": "NVML, 10 ms polling"}
 
 
 def measured_peaks():
@@ -254,6 +275,18 @@ def main():
            "h2d_bytes_per_step": sum(x.numel() * 4 for x in h_in), "d2h_bytes_per_step": sum(o.numel() * 4 for o in h_out),
            "api": "rosenna_use_model_f32 (host arrays, pinned)"}
     ok_out = bool(torch.isfinite(h_out[0]).all())
+    # the link's own ceiling for this step: a plain pinned H2D copy of the same inputs
+    d_tmp = [torch.empty_like(x) for x in ins]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(3):
+        for dst, src in zip(d_tmp, h_in):
+            dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    h2d_gbs = 3 * e2e["h2d_bytes_per_step"] / (time.perf_counter() - t0) / 1e9
+    e2e["plain_h2d_gbs"] = h2d_gbs
+    e2e["h2d_bound_samples_s"] = h2d_gbs * 1e9 / (e2e["h2d_bytes_per_step"] / n) * world
+    del d_tmp
 
     # ---- roofline of the dominant kernel ----
     kernel_s = t_dev / max(1, args.steps * launches_per_step) if launches_per_step == 1 else None

@@ -15,11 +15,18 @@
 //             holds all gates of two units and updates their cell state in
 //             registers; h_t goes back to shared memory for step t+1.
 // conv_pool : direct convolution (layers.f90:183-233) + ReLU + max/avg pool
-//             (layers.f90:236-310) with zero padding, one thread per sample
-//             and pooled output element.
+//             (layers.f90:236-310) with zero padding.  The tiled kernel (stride
+//             1, 3x3 kernels, pool windows up to 2x2) gives each lane one sample
+//             and each warp a (pooled position, 8 or 16 output channels) item:
+//             the input patch of the pool window sits in registers, the weights
+//             are broadcast from shared memory, and every pool-window conv
+//             output of every channel in the group accumulates in registers.
+//             Other shapes use one thread per sample and pooled element.
 #include "kernels.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 
 namespace rosenna {
 
@@ -370,6 +377,97 @@ __device__ __forceinline__ float conv_value(const ConvArgs &p, const float *in, 
     return p.relu ? (acc < 0.f ? 0.f : acc) : acc;
 }
 
+// Lane = sample (32 consecutive samples per warp, coalesced rows), warp = a
+// stream of (pooled position, channel group) items.  Shared memory holds the
+// weights as [ic][kh][kw][oc] (oc fastest, OCp = OC rounded up to OCB) and the
+// bias, so each (ic, kh, kw) step reads OCB weights with OCB/4 broadcast loads.
+// Semantics are those of conv_pool_kernel below: conv zero padding by skipping,
+// pool-window positions outside the conv output count as 0.
+template <int KS, int PK, int OCB>
+__global__ void __launch_bounds__(256) conv_pool_tile_kernel(const ConvArgs p) {
+    extern __shared__ float sw[];
+    constexpr int P = PK - 1 + KS;  // input patch side of one pool window
+    const int OCp = (p.OC + OCB - 1) / OCB * OCB;
+    const int nw = p.C * KS * KS * OCp;
+    for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+        const int oc = i % OCp, r = i / OCp;  // r = (ic*KS + kh)*KS + kw
+        sw[i] = oc < p.OC ? p.arena[p.w_off + (long long)oc * p.C * KS * KS + r] : 0.f;
+    }
+    for (int i = threadIdx.x; i < OCp; i += blockDim.x) sw[nw + i] = i < p.OC ? p.arena[p.b_off + i] : 0.f;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const long long s = (long long)blockIdx.x * 32 + lane;
+    const bool valid = s < p.n;
+    const float *in = p.in + (valid ? s : 0);
+    const int ngrp = OCp / OCB, items = p.Hq * p.Wq * ngrp;
+    for (int item = warp; item < items; item += nwarps) {
+        const int grp = item % ngrp, pos = item / ngrp, ph = pos % p.Hq, pw = pos / p.Hq;
+        const int ch0 = PK > 1 ? ph * p.pstr_h - p.ppad_h : ph, cw0 = PK > 1 ? pw * p.pstr_w - p.ppad_w : pw;
+        const int ih0 = ch0 - p.pad_h, iw0 = cw0 - p.pad_w;
+        float acc[PK][PK][OCB];
+#pragma unroll
+        for (int a = 0; a < PK; a++)
+#pragma unroll
+            for (int b = 0; b < PK; b++)
+#pragma unroll
+                for (int o = 0; o < OCB; o++) acc[a][b][o] = 0.f;
+        const float *wg = sw + grp * OCB;
+#pragma unroll 1
+        for (int ic = 0; ic < p.C; ic++) {
+            float x[P][P];
+#pragma unroll
+            for (int a = 0; a < P; a++)
+#pragma unroll
+                for (int b = 0; b < P; b++) {
+                    const int ih = ih0 + a, iw = iw0 + b;
+                    x[a][b] = (valid && ih >= 0 && ih < p.Hin && iw >= 0 && iw < p.Win)
+                                  ? __ldg(in + (long long)(ic + p.C * (ih + p.Hin * iw)) * p.ld_in)
+                                  : 0.f;
+                }
+#pragma unroll
+            for (int kh = 0; kh < KS; kh++)
+#pragma unroll
+                for (int kw = 0; kw < KS; kw++) {
+                    const float4 *w4 = reinterpret_cast<const float4 *>(wg + ((ic * KS + kh) * KS + kw) * OCp);
+#pragma unroll
+                    for (int o4 = 0; o4 < OCB / 4; o4++) {
+                        const float4 w = w4[o4];
+#pragma unroll
+                        for (int a = 0; a < PK; a++)
+#pragma unroll
+                            for (int b = 0; b < PK; b++) {
+                                const float xv = x[a + kh][b + kw];
+                                acc[a][b][4 * o4 + 0] = fmaf(w.x, xv, acc[a][b][4 * o4 + 0]);
+                                acc[a][b][4 * o4 + 1] = fmaf(w.y, xv, acc[a][b][4 * o4 + 1]);
+                                acc[a][b][4 * o4 + 2] = fmaf(w.z, xv, acc[a][b][4 * o4 + 2]);
+                                acc[a][b][4 * o4 + 3] = fmaf(w.w, xv, acc[a][b][4 * o4 + 3]);
+                            }
+                    }
+                }
+        }
+#pragma unroll
+        for (int o = 0; o < OCB; o++) {
+            const int oc = grp * OCB + o;
+            if (oc >= p.OC) break;
+            const float bias = sw[nw + oc];
+            float best = -INFINITY, sum = 0.f;
+#pragma unroll
+            for (int a = 0; a < PK; a++)
+#pragma unroll
+                for (int b = 0; b < PK; b++) {
+                    const int ch = ch0 + a, cw = cw0 + b;
+                    float v = acc[a][b][o] + bias;
+                    if (p.relu) v = v < 0.f ? 0.f : v;
+                    if (ch < 0 || ch >= p.Ho || cw < 0 || cw >= p.Wo) v = 0.f;  // zero-padded pool input
+                    best = fmaxf(best, v);
+                    sum += v;
+                }
+            const float y = PK == 1 ? sum : (p.pool == 1 ? best : sum / (float)(PK * PK));
+            if (valid) p.out[(long long)(oc * p.so_c + ph * p.so_h + pw * p.so_w) * p.ld_out + s] = y;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(128) conv_pool_kernel(const ConvArgs p) {
     const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= p.n) return;
@@ -483,9 +581,32 @@ cudaError_t launch_lstm(LstmArgs a, int num_sms, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+template <int KS, int PK, int OCB>
+static cudaError_t launch_conv_tile(const ConvArgs &a, cudaStream_t st) {
+    const int OCp = (a.OC + OCB - 1) / OCB * OCB;
+    const size_t bytes = sizeof(float) * ((size_t)a.C * KS * KS * OCp + OCp);
+    const long long tiles = (a.n + 31) / 32;
+    if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    conv_pool_tile_kernel<KS, PK, OCB><<<(unsigned)tiles, 256, bytes, st>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
     const long long outs = (long long)a.OC * a.Hq * a.Wq;
     if (a.n <= 0 || outs <= 0) return cudaSuccess;
+    // the tiled kernel: stride-1 3x3 convolution, no pool or a 2x2 pool window
+    // (weights and bias within the default 48 KB of dynamic shared memory);
+    // ROSENNA_CONV_PATH=direct keeps every convolution on the per-element kernel
+    static const bool direct_only = [] {
+        const char *e = getenv("ROSENNA_CONV_PATH");
+        return e && std::string(e) == "direct";
+    }();
+    if (!direct_only && a.conv && a.KS == 3 && a.str_h == 1 && a.str_w == 1 && (a.pool == 0 || a.pk == 2) &&
+        ((size_t)a.C * 9 + 1) * ((a.OC + 15) / 16 * 16) * sizeof(float) <= 48 * 1024) {
+        const bool wide = a.OC > 8;
+        if (a.pool == 0) return wide ? launch_conv_tile<3, 1, 16>(a, st) : launch_conv_tile<3, 1, 8>(a, st);
+        return wide ? launch_conv_tile<3, 2, 16>(a, st) : launch_conv_tile<3, 2, 8>(a, st);
+    }
     if (outs > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((a.n + 127) / 128), (unsigned)outs);
     conv_pool_kernel<<<grid, 128, 0, st>>>(a);

@@ -325,7 +325,11 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
     const Plan &P = g_ctx.plan;
     const int64_t total = b - a;
     if (total <= 0) return Status::Ok();
-    const int64_t chunk = std::min<int64_t>(max_chunk(total), (int64_t)1 << 20);
+    // at least four chunks (of >= 16384 samples) so that one stream's copies
+    // overlap the other stream's kernels; at most 2^20 samples per chunk
+    int64_t chunk = std::min<int64_t>(max_chunk(total), (int64_t)1 << 20);
+    chunk = std::min(chunk, std::max<int64_t>(16384, (total + 3) / 4));
+    chunk = (chunk + 31) / 32 * 32;
     for (int k = 0; k < kSlots; k++) {
         Status st = ensure_scratch(d.slots[k], std::min(chunk, total));
         if (!st.ok()) return st;

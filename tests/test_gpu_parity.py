@@ -2,6 +2,8 @@
 golden fixtures.  Tolerance, per element: |gpu - ref| <= 1e-5 + 1e-4 * |ref|
 (fp32 engine against fp64 reference; the reference's own checker uses an
 absolute 1e-5, test/testChecker.py:14-17)."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -13,6 +15,7 @@ from tests import goldens
 pytestmark = pytest.mark.gpu
 
 ABS, REL = 1e-5, 1e-4
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def assert_close(out, ref, what=""):
@@ -147,6 +150,37 @@ def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
         out = api.use_model_rows(ins)[0]
         ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
         assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
+
+
+@pytest.mark.parametrize("conv_path", ["tiled", "direct"])
+def test_cnn_conv_paths(conv_path, tmp_path):
+    """The tiled conv+pool kernel and the per-element one on the CNN workload and
+    the small golden CNN (run in a child process: the path is fixed at load)."""
+    import subprocess, sys, textwrap
+    code = textwrap.dedent(f"""
+        import sys
+        sys.path.insert(0, {repr(ROOT)})
+        from rosenna_b200 import api, workloads
+        from oracle.oracle import OracleModel
+        from tests import goldens
+        from tests.test_gpu_parity import assert_close
+        api.set_devices([0])
+        workloads.write_model('cnn', {repr(str(tmp_path))})
+        api.initialize({repr(str(tmp_path))})
+        for n in (1, 37, 1000):
+            ins = workloads.make_inputs('cnn', n, seed_offset=11 + n)
+            out = api.use_model_rows(ins)[0]
+            ref = OracleModel({repr(str(tmp_path))}).run_batched(n, ins, [1], [1])[0]
+            assert_close(out, ref.reshape(out.shape), f'cnn {conv_path} n={{n}}')
+        d = goldens.case_dir('cnn_small')
+        api.initialize(d)
+        out = api.use_model(goldens.inputs('cnn_small'), n=1)[0]
+        assert_close(out, goldens.golden('cnn_small'), 'cnn_small {conv_path}')
+        print('ok')
+    """)
+    env = dict(os.environ, ROSENNA_CONV_PATH=conv_path)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
 
 
 @pytest.mark.parametrize("tail", ["1", "0"])
