@@ -17,7 +17,7 @@
 // conv_pool : direct convolution (layers.f90:183-233) + ReLU + max/avg pool
 //             (layers.f90:236-310) with zero padding.  The tiled kernel (stride
 //             1, 3x3 kernels, pool windows up to 2x2) gives each lane one sample
-//             and each warp a (pooled position, 8 or 16 output channels) item:
+//             and each warp a (pooled position, 8 output channels) item:
 //             the input patch of the pool window sits in registers, the weights
 //             are broadcast from shared memory, and every pool-window conv
 //             output of every channel in the group accumulates in registers.
@@ -384,7 +384,7 @@ __device__ __forceinline__ float conv_value(const ConvArgs &p, const float *in, 
 // Semantics are those of conv_pool_kernel below: conv zero padding by skipping,
 // pool-window positions outside the conv output count as 0.
 template <int KS, int PK, int OCB>
-__global__ void __launch_bounds__(256) conv_pool_tile_kernel(const ConvArgs p) {
+__global__ void __launch_bounds__(256, 2) conv_pool_tile_kernel(const ConvArgs p) {
     extern __shared__ float sw[];
     constexpr int P = PK - 1 + KS;  // input patch side of one pool window
     const int OCp = (p.OC + OCB - 1) / OCB * OCB;
@@ -397,13 +397,17 @@ __global__ void __launch_bounds__(256) conv_pool_tile_kernel(const ConvArgs p) {
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const long long s = (long long)blockIdx.x * 32 + lane;
+    const bool full = (long long)blockIdx.x * 32 + 32 <= p.n;  // all 32 lanes hold a sample (warp-uniform)
     const bool valid = s < p.n;
     const float *in = p.in + (valid ? s : 0);
+    const long long sa = (long long)p.C * p.ld_in, sb = (long long)p.C * p.Hin * p.ld_in;  // +1 in h, +1 in w
     const int ngrp = OCp / OCB, items = p.Hq * p.Wq * ngrp;
     for (int item = warp; item < items; item += nwarps) {
         const int grp = item % ngrp, pos = item / ngrp, ph = pos % p.Hq, pw = pos / p.Hq;
         const int ch0 = PK > 1 ? ph * p.pstr_h - p.ppad_h : ph, cw0 = PK > 1 ? pw * p.pstr_w - p.ppad_w : pw;
         const int ih0 = ch0 - p.pad_h, iw0 = cw0 - p.pad_w;
+        // the whole patch inside the input and every lane a sample: no checks
+        const bool inner = full && ih0 >= 0 && ih0 + P <= p.Hin && iw0 >= 0 && iw0 + P <= p.Win;
         float acc[PK][PK][OCB];
 #pragma unroll
         for (int a = 0; a < PK; a++)
@@ -412,18 +416,27 @@ __global__ void __launch_bounds__(256) conv_pool_tile_kernel(const ConvArgs p) {
 #pragma unroll
                 for (int o = 0; o < OCB; o++) acc[a][b][o] = 0.f;
         const float *wg = sw + grp * OCB;
+        const float *pin = inner ? in + (long long)p.C * (ih0 + p.Hin * iw0) * p.ld_in : in;
 #pragma unroll 1
         for (int ic = 0; ic < p.C; ic++) {
             float x[P][P];
+            if (inner) {
+                const float *q = pin + (long long)ic * p.ld_in;
 #pragma unroll
-            for (int a = 0; a < P; a++)
+                for (int b = 0; b < P; b++)
 #pragma unroll
-                for (int b = 0; b < P; b++) {
-                    const int ih = ih0 + a, iw = iw0 + b;
-                    x[a][b] = (valid && ih >= 0 && ih < p.Hin && iw >= 0 && iw < p.Win)
-                                  ? __ldg(in + (long long)(ic + p.C * (ih + p.Hin * iw)) * p.ld_in)
-                                  : 0.f;
-                }
+                    for (int a = 0; a < P; a++) x[a][b] = __ldg(q + a * sa + b * sb);
+            } else {
+#pragma unroll
+                for (int a = 0; a < P; a++)
+#pragma unroll
+                    for (int b = 0; b < P; b++) {
+                        const int ih = ih0 + a, iw = iw0 + b;
+                        x[a][b] = (valid && ih >= 0 && ih < p.Hin && iw >= 0 && iw < p.Win)
+                                      ? __ldg(in + (long long)(ic + p.C * (ih + p.Hin * iw)) * p.ld_in)
+                                      : 0.f;
+                    }
+            }
 #pragma unroll
             for (int kh = 0; kh < KS; kh++)
 #pragma unroll
@@ -445,6 +458,9 @@ __global__ void __launch_bounds__(256) conv_pool_tile_kernel(const ConvArgs p) {
                     }
                 }
         }
+        // pool-window positions outside the conv output count as 0 (zero-padded pool input)
+        const bool win_inside = ch0 >= 0 && ch0 + PK <= p.Ho && cw0 >= 0 && cw0 + PK <= p.Wo;
+        float *po = p.out + (long long)(ph * p.so_h + pw * p.so_w) * p.ld_out + s;
 #pragma unroll
         for (int o = 0; o < OCB; o++) {
             const int oc = grp * OCB + o;
@@ -455,15 +471,14 @@ __global__ void __launch_bounds__(256) conv_pool_tile_kernel(const ConvArgs p) {
             for (int a = 0; a < PK; a++)
 #pragma unroll
                 for (int b = 0; b < PK; b++) {
-                    const int ch = ch0 + a, cw = cw0 + b;
                     float v = acc[a][b][o] + bias;
                     if (p.relu) v = v < 0.f ? 0.f : v;
-                    if (ch < 0 || ch >= p.Ho || cw < 0 || cw >= p.Wo) v = 0.f;  // zero-padded pool input
+                    if (!win_inside && (ch0 + a < 0 || ch0 + a >= p.Ho || cw0 + b < 0 || cw0 + b >= p.Wo)) v = 0.f;
                     best = fmaxf(best, v);
                     sum += v;
                 }
-            const float y = PK == 1 ? sum : (p.pool == 1 ? best : sum / (float)(PK * PK));
-            if (valid) p.out[(long long)(oc * p.so_c + ph * p.so_h + pw * p.so_w) * p.ld_out + s] = y;
+            const float y = PK == 1 ? sum : (p.pool == 1 ? best : sum * (1.f / (float)(PK * PK)));
+            if (valid) po[(long long)oc * p.so_c * p.ld_out] = y;
         }
     }
 }
@@ -602,10 +617,10 @@ cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
         return e && std::string(e) == "direct";
     }();
     if (!direct_only && a.conv && a.KS == 3 && a.str_h == 1 && a.str_w == 1 && (a.pool == 0 || a.pk == 2) &&
-        ((size_t)a.C * 9 + 1) * ((a.OC + 15) / 16 * 16) * sizeof(float) <= 48 * 1024) {
-        const bool wide = a.OC > 8;
-        if (a.pool == 0) return wide ? launch_conv_tile<3, 1, 16>(a, st) : launch_conv_tile<3, 1, 8>(a, st);
-        return wide ? launch_conv_tile<3, 2, 16>(a, st) : launch_conv_tile<3, 2, 8>(a, st);
+        ((size_t)a.C * 9 + 1) * ((a.OC + 7) / 8 * 8) * sizeof(float) <= 48 * 1024) {
+        // 8 output channels per item: two CTAs per SM fit (16 per item spills or halves occupancy)
+        if (a.pool == 0) return launch_conv_tile<3, 1, 8>(a, st);
+        return launch_conv_tile<3, 2, 8>(a, st);
     }
     if (outs > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((a.n + 127) / 128), (unsigned)outs);
