@@ -406,7 +406,7 @@ __device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc
 // 1 hands its partial sums to group 0 through shared memory, and group 0 adds
 // bias, applies the activation and writes the row.
 template <int NP>
-__device__ __noinline__ bool run_tail(const TcArgs &p, uint8_t *base, uint32_t lane_base, int g, int r, int t,
+__device__ __forceinline__ bool run_tail(const TcArgs &p, uint8_t *base, uint32_t lane_base, int g, int r, int t,
                                       int np_prev, uint32_t &xt, int slot) {
     const float *stail = reinterpret_cast<const float *>(base + kSmemB + kSmemA + kSmemBias);
     float *sx = reinterpret_cast<float *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW);
