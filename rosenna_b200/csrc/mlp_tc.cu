@@ -178,6 +178,16 @@ __device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) 
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Two fp32 lanes per instruction (sm_100 packed f32x2, round to nearest):
+// (a0, a1) += (bits b0, b1).  Same results as two scalar FADDs in half the
+// issue slots.
+__device__ __forceinline__ void add2(float &a0, float &a1, uint32_t b0, uint32_t b1) {
+    asm("{\n\t.reg .b64 a, b;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\t"
+        "add.rn.f32x2 a, a, b;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(b0), "r"(b1));
+}
+
 // K-major operand, 128-byte swizzle: 8-row atoms of 1024 bytes (SBO), rows of
 // 128 bytes; LBO unused for swizzled K-major (set to 16 bytes); version 1.
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
@@ -360,29 +370,20 @@ __device__ __forceinline__ bool issue_in_turn(const TcArgs &p, uint8_t *a0, uint
     return true;
 }
 
-// Adds bias, applies the activation and writes this group's half of the layer
-// output: into TMEM T for the next layer, or to global memory.  Columns at and
-// beyond N hold act(0) (their weight rows and bias are zero padding) and meet
-// zero weight columns in the next layer, so they need no masking.  The code is
-// kept short: it runs once per layer and is fetched cold each time.
+// Applies the activation (the accumulators started at the bias) and writes
+// this group's half of the layer output: into TMEM T for the next layer, or to
+// global memory.  Columns at and beyond N hold act(0) (their weight rows and
+// bias are zero padding) and meet zero weight columns in the next layer, so
+// they need no masking.  The code is kept short: it runs once per layer.
 template <int ACT>
-__device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc)[128], const float *bias, int N, int g,
+__device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc)[128], int N, int g,
                                               uint32_t lane_base, bool last, int t, int r) {
     if (!last) {
 #pragma unroll
         for (int q = 0; q < 8; q++) {
             float v[16];
 #pragma unroll
-            for (int e4 = 0; e4 < 4; e4++) {
-                const float4 b4 = reinterpret_cast<const float4 *>(bias)[4 * q + e4];
-                const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int i = 16 * q + 4 * e4 + e;
-                    const float y = tc_act<ACT>(acc[i] + bb[e]);
-                    v[4 * e4 + e] = 128 * g + i < N ? y : 0.f;
-                }
-            }
+            for (int e = 0; e < 16; e++) v[e] = tc_act<ACT>(acc[16 * q + e]);
             tmem_st16(lane_base + kTCol + (uint32_t)(128 * g + 16 * q), v);
         }
     } else {
@@ -394,47 +395,54 @@ __device__ __forceinline__ void finalize_half(const TcArgs &p, const float (&acc
                 if (128 * g + q0 < N) {
 #pragma unroll
                     for (int q = q0; q < q0 + 16; q++)
-                        if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act<ACT>(acc[q] + bias[q]);
+                        if (128 * g + q < N) o[(long long)q * p.ld_out] = tc_act<ACT>(acc[q]);
                 }
         }
     }
 }
 
 // The last layer on the CUDA cores (fp32 FMA), for a narrow output (N <= 16)
-// whose MMA chunks would be latency-bound: each thread takes the dot products
-// of its row over its group's K half (its own T columns, below np_prev), group
-// 1 hands its partial sums to group 0 through shared memory, and group 0 adds
-// bias, applies the activation and writes the row.
+// whose MMA chunks would be latency-bound.  tail_dots: this thread's dot
+// products over its group's K half, straight from the accumulators of the
+// layer before (no TMEM round trip): o[n] = sum over the group's columns
+// k < np_prev of act(acc[k]) * W^T[k][n].
+template <int ACT, int NP>
+__device__ __forceinline__ void tail_dots(float (&o)[NP], const float (&acc)[128], const float *stail, int g,
+                                          int np_prev) {
+#pragma unroll
+    for (int n = 0; n < NP; n++) o[n] = 0.f;
+    const uint32_t w_base = smem_u32(stail + 128 * g * kTcTailMaxN);
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        if (128 * g + 16 * q >= np_prev) break;
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            const float x = tc_act<ACT>(acc[16 * q + e]);
+            const uint32_t w_row = w_base + (uint32_t)((16 * q + e) * kTcTailMaxN * 4);
+#pragma unroll
+            for (int n4 = 0; n4 < NP / 4; n4++) {
+                float4 w4;
+                asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                             : "=f"(w4.x), "=f"(w4.y), "=f"(w4.z), "=f"(w4.w)
+                             : "r"(w_row + 16u * n4));
+                o[4 * n4 + 0] = fmaf(x, w4.x, o[4 * n4 + 0]);
+                o[4 * n4 + 1] = fmaf(x, w4.y, o[4 * n4 + 1]);
+                o[4 * n4 + 2] = fmaf(x, w4.z, o[4 * n4 + 2]);
+                o[4 * n4 + 3] = fmaf(x, w4.w, o[4 * n4 + 3]);
+            }
+        }
+    }
+}
+
+// run_tail: group 1 hands its partial sums to group 0 through shared memory,
+// and group 0 adds bias, applies the activation and writes the row.
 template <int NP>
-__device__ __forceinline__ bool run_tail(const TcArgs &p, uint8_t *base, uint32_t lane_base, int g, int r, int t,
-                                      int np_prev, uint32_t &xt, int slot) {
-    const float *stail = reinterpret_cast<const float *>(base + kSmemB + kSmemA + kSmemBias);
+__device__ __forceinline__ bool run_tail(const TcArgs &p, uint8_t *base, float (&o)[NP], int g, int r, int t,
+                                         uint32_t &xt, int slot) {
     float *sx = reinterpret_cast<float *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW);
     const float *btail = reinterpret_cast<const float *>(base + kSmemB + kSmemA) + p.nlayers * kNMax;
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
     uint64_t *x_full = bars + 12, *x_empty = bars + 13;
-    float o[NP];
-#pragma unroll
-    for (int n = 0; n < NP; n++) o[n] = 0.f;
-#pragma unroll 1
-    for (int q = 0; q < 8; q++) {
-        const int k0 = 128 * g + 16 * q;
-        if (k0 >= np_prev) break;
-        float v[16];
-        tmem_ld16(lane_base + kTCol + (uint32_t)k0, v);
-#pragma unroll
-        for (int e = 0; e < 16; e++) {
-            const float4 *w = reinterpret_cast<const float4 *>(stail + (k0 + e) * kTcTailMaxN);
-#pragma unroll
-            for (int n4 = 0; n4 < NP / 4; n4++) {
-                const float4 w4 = w[n4];
-                o[4 * n4 + 0] = fmaf(v[e], w4.x, o[4 * n4 + 0]);
-                o[4 * n4 + 1] = fmaf(v[e], w4.y, o[4 * n4 + 1]);
-                o[4 * n4 + 2] = fmaf(v[e], w4.z, o[4 * n4 + 2]);
-                o[4 * n4 + 3] = fmaf(v[e], w4.w, o[4 * n4 + 3]);
-            }
-        }
-    }
     if (p.tail_k > 128) {  // both groups hold K columns: combine the halves
         if (g == 1) {
             if (!mbar_wait(x_empty, (xt & 1) ^ 1, p.err, 10, t, (int)xt, 0, slot)) return false;
@@ -555,8 +563,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
         for (int l = 0; l < nl && ok; l++) {
             const int nch = p.L[l].nch, Np = p.L[l].Np;
             const bool has_half = 128 * g < Np;
-#pragma unroll
-            for (int q = 0; q < 128; q++) acc[q] = 0.f;
             const bool both = Np > 128;  // the halves take turns in the tensor pipe
             if (halves) {
                 stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 0, j);
@@ -566,6 +572,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                 ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi,
                                    ts, both);
             ok = __all_sync(0xffffffffu, ok);
+            {  // while chunk 0 computes: the accumulators start at the bias (zero beyond Np)
+                const uint32_t b_addr = smem_u32(sbias + l * kNMax + 128 * g);
+#pragma unroll
+                for (int q = 0; q < 32; q++)
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
+                                 : "r"(b_addr + 16u * q));
+            }
             for (int c = 0; c < nch && ok; c++) {
                 const uint32_t jj = j + (uint32_t)c;
                 const int s = jj & 1;
@@ -588,7 +602,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                             for (int u = 0; u < 4; u++)
                                 if (128 * g + 16 * (q0 + u) < Np) {
 #pragma unroll
-                                    for (int e = 0; e < 16; e++) acc[16 * (q0 + u) + e] += __uint_as_float(v[u][e]);
+                                    for (int e = 0; e < 16; e += 2)
+                                        add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e], v[u][e + 1]);
                                 }
                         }
                     }
@@ -620,20 +635,35 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             if (!ok) break;
             const bool last = l + 1 == nl;
             const bool to_out = last && p.tail_n == 0;  // else T, for the next layer or the tail
-            if (has_half) {
-                const float *bias = sbias + l * kNMax + 128 * g;
-                switch (p.L[l].act) {
-                    case 1: finalize_half<1>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
-                    case 2: finalize_half<2>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
-                    case 3: finalize_half<3>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
-                    default: finalize_half<0>(p, acc, bias, p.L[l].N, g, lane_base, to_out, t, r); break;
+            if (last && !to_out) {  // the CUDA-core tail takes this layer's activations from acc
+                const float *stail = reinterpret_cast<const float *>(base + kSmemB + kSmemA + kSmemBias);
+                const int np_prev = has_half ? Np : 0;
+                if (p.tail_np == 8) {
+                    float o[8];
+                    switch (p.L[l].act) {
+                        case 1: tail_dots<1, 8>(o, acc, stail, g, np_prev); break;
+                        case 2: tail_dots<2, 8>(o, acc, stail, g, np_prev); break;
+                        case 3: tail_dots<3, 8>(o, acc, stail, g, np_prev); break;
+                        default: tail_dots<0, 8>(o, acc, stail, g, np_prev); break;
+                    }
+                    ok = run_tail<8>(p, base, o, g, r, t, xt, slot);
+                } else {
+                    float o[16];
+                    switch (p.L[l].act) {
+                        case 1: tail_dots<1, 16>(o, acc, stail, g, np_prev); break;
+                        case 2: tail_dots<2, 16>(o, acc, stail, g, np_prev); break;
+                        case 3: tail_dots<3, 16>(o, acc, stail, g, np_prev); break;
+                        default: tail_dots<0, 16>(o, acc, stail, g, np_prev); break;
+                    }
+                    ok = run_tail<16>(p, base, o, g, r, t, xt, slot);
                 }
-            }
-            if (last && !to_out) {
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                ok = p.tail_np == 8 ? run_tail<8>(p, base, lane_base, g, r, t, has_half ? Np : 0, xt, slot)
-                                    : run_tail<16>(p, base, lane_base, g, r, t, has_half ? Np : 0, xt, slot);
+            } else if (has_half) {
+                switch (p.L[l].act) {
+                    case 1: finalize_half<1>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    case 2: finalize_half<2>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    case 3: finalize_half<3>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    default: finalize_half<0>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                }
             }
             if (!last) {
                 // the next layer stages K halves that the other group wrote: hand T over
