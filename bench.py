@@ -32,7 +32,11 @@ sys.path.insert(0, ROOT)
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
 # capture summarised in profiles/ (None until captured).
-NCU_TRAFFIC = {}
+# DRAM bytes (read + write) per sample of the dominant kernel, from the
+# committed ncu captures (profiles/); scaled by the batch for `traffic`
+NCU_TRAFFIC_PER_SAMPLE = {
+    ("wide_mlp", "mlp_tc_kernel"): (69.478144e6 + 9.841664e6) / 1048576,
+}
 
 DEFAULT_WORKLOAD = "wide_mlp"
 
@@ -308,7 +312,9 @@ def main():
                 "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
                 "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
                 "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (MEASURED_PEAKS.json has no FP32 figure)"}
-    roof["traffic"] = NCU_TRAFFIC.get((args.workload, roof["kernel"]))
+    per_sample = NCU_TRAFFIC_PER_SAMPLE.get((args.workload, roof["kernel"]))
+    roof["traffic"] = per_sample * n if per_sample else None
+    roof["traffic_unit"] = "bytes per launch (ncu capture at a smaller batch, scaled by samples)"
     roof["algorithmic_flops_per_launch"] = w.flops_per_sample * n if kernel_s else None
 
     if rank == 0:
