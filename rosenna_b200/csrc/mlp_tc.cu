@@ -76,6 +76,9 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
@@ -370,6 +373,31 @@ __device__ __forceinline__ bool issue_in_turn(const TcArgs &p, uint8_t *a0, uint
     return true;
 }
 
+// Layer hand-over by group 0 (which owns columns 0..127): applies the
+// activation in place, stages A chunk C0/32 of the next layer (columns
+// C0..C0+31) straight from the registers into ring slot j&1, and arrives on its
+// a_full for the six staging warps (warps 0 and 1 count twice: 64*2 + 64 = 192).
+template <int ACT>
+__device__ __forceinline__ void act_in_place(float (&acc)[128]) {
+#pragma unroll
+    for (int i = 0; i < 128; i++) acc[i] = tc_act<ACT>(acc[i]);
+}
+template <int C0>
+__device__ __forceinline__ void stage_from_regs(uint8_t *a0, uint64_t *a_full, int r, int warp, const float (&acc)[128],
+                                                uint32_t j) {
+    uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++) v[e] = acc[C0 + 16 * h + e];
+        put_a16(ahi, ahi + kATile, r, 16 * h, v);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    mbar_arrive_n(&a_full[j & 1], warp < 2 ? 2u : 1u);
+}
+
 // Applies the activation (the accumulators started at the bias) and writes
 // this group's half of the layer output: into TMEM T for the next layer, or to
 // global memory.  Columns at and beyond N hold act(0) (their weight rows and
@@ -564,13 +592,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             const int nch = p.L[l].nch, Np = p.L[l].Np;
             const bool has_half = 128 * g < Np;
             const bool both = Np > 128;  // the halves take turns in the tensor pipe
-            if (halves) {
-                stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 0, j);
-                if (nch > 1) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 1, j + 1);
+            if (l == 0) {  // the input layer: chunks 0 and 1 from global memory
+                if (halves) {
+                    stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 0, j);
+                    if (nch > 1) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 1, j + 1);
+                }
+                if (has_half && issuer)
+                    ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi,
+                                       ts, both);
+            } else if (g == 1 && has_half && issuer) {
+                // group 0 staged chunks 0 and 1 from its registers and issued chunk 0 at
+                // the previous layer's end; group 1's half of chunk 0 follows it
+                ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi, ts,
+                                   both);
             }
-            if (has_half && issuer)
-                ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi,
-                                   ts, both);
             ok = __all_sync(0xffffffffu, ok);
             {  // while chunk 0 computes: the accumulators start at the bias (zero beyond Np)
                 const uint32_t b_addr = smem_u32(sbias + l * kNMax + 128 * g);
@@ -619,6 +654,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                 } else if (issuer) {
                     umma_commit(&a_empty[s]);  // a group without columns in this layer releases the stage at once
                 }
+                if (c == 0 && l > 0) {  // T of the previous layer: both halves written (before chunk 2 is staged)
+                    ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, l, (int)tb, (int)j, slot));
+                    tb++;
+                    tc_fence_after();
+                    if (!ok) break;
+                }
+                // group 0 takes the last chunk's a_empty at the hand-over to the next layer
+                if (g == 0 && c == nch - 1 && l + 1 < nl) break;
                 // Every thread observes the consumption of every chunk in order, so every
                 // later wait on any ring barrier is at most one phase ahead: no aliasing.
                 ok = __all_sync(0xffffffffu,
@@ -657,22 +700,58 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                     }
                     ok = run_tail<16>(p, base, o, g, r, t, xt, slot);
                 }
-            } else if (has_half) {
+            } else if (!last && g == 0) {
+                // Hand-over by group 0: chunks 0 and 1 of the next layer straight from
+                // the registers, chunk 0 issued at once (behind group 1's last MMAs),
+                // columns 64..127 into T for the staging warps.
                 switch (p.L[l].act) {
-                    case 1: finalize_half<1>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
-                    case 2: finalize_half<2>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
-                    case 3: finalize_half<3>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
-                    default: finalize_half<0>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    case 1: act_in_place<1>(acc); break;
+                    case 2: act_in_place<2>(acc); break;
+                    case 3: act_in_place<3>(acc); break;
+                    default: break;
                 }
-            }
-            if (!last) {
-                // the next layer stages K halves that the other group wrote: hand T over
+                const int nl1 = l + 1;
+                stage_from_regs<0>(a0, a_full, r, warp, acc, j);
+                if (issuer)
+                    ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, 0, nl1, 0, j,
+                                       pi, ts, p.L[nl1].Np > 128);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+#pragma unroll
+                for (int q = 4; q < 8; q++) {
+                    float v[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) v[e] = acc[16 * q + e];
+                    tmem_st16(lane_base + kTCol + (uint32_t)(16 * q), v);
+                }
+                // the last chunk of this layer (its slot takes chunk 1 of the next)
+                const uint32_t jl = j - 1;
+                ok = __all_sync(0xffffffffu, mbar_wait(&a_empty[jl & 1], (jl >> 1) & 1, p.err, 5,
+                                                       (l << 8) | (nch - 1), (int)jl, (int)pu, slot));
+                if (!ok) break;
+                if (loader) {
+                    b_done = jl + 1;
+                    int t2 = t, l2 = l, c2 = nch - 1;
+                    if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, b_issued++);
+                }
+                if (p.L[nl1].nch > 1) stage_from_regs<32>(a0, a_full, r, warp, acc, j + 1);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 mbar_arrive(t_ready);
-                ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, l, (int)tb, (int)j, slot));
-                tb++;
-                tc_fence_after();
+            } else if (has_half || !last) {
+                if (has_half) {
+                    switch (p.L[l].act) {
+                        case 1: finalize_half<1>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                        case 2: finalize_half<2>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                        case 3: finalize_half<3>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                        default: finalize_half<0>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                    }
+                }
+                if (!last) {  // group 1: its half of T for the next layer
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    mbar_arrive(t_ready);
+                }
             }
         }
     }
