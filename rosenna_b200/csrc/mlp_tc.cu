@@ -356,20 +356,24 @@ __device__ __forceinline__ bool issue_chunk(const TcArgs &p, uint8_t *a0, uint8_
     return true;
 }
 
-// issue_chunk in the halves' turn order: where both halves have columns, group
-// 1 issues chunk jj only after group 0 has issued it, so the two halves' MMAs
-// alternate in the tensor pipe and one half drains while the other computes.
+// issue_chunk in the halves' turn order: group 1 takes chunk jj only after
+// group 0 has issued it, so the two halves' MMAs alternate in the tensor pipe
+// and one half drains while the other computes.  Group 0 issues every chunk and
+// arrives on turn[jj&1]; group 1 waits there for every chunk (also one it has
+// no columns of).  Two barriers by chunk parity: group 0 cannot issue chunk
+// jj+2 before group 1 issued jj (the A stage of jj+2 is staged only after
+// chunk jj is consumed), so neither barrier gets a phase ahead of its waiter.
+__device__ __forceinline__ bool wait_turn(const TcArgs &p, uint64_t *turn, int l, int c, uint32_t jj) {
+    return mbar_wait(&turn[jj & 1], (jj >> 1) & 1, p.err, 8, (l << 8) | c, (int)jj, 0, 0);
+}
 __device__ __forceinline__ bool issue_in_turn(const TcArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
                                               uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full,
                                               uint64_t *p_empty, uint64_t *turn, uint32_t tmem, int g, int l, int c,
-                                              uint32_t jj, uint32_t &pi, uint32_t &ts, bool both) {
-    if (g == 1 && both) {
-        if (!mbar_wait(turn, ts & 1, p.err, 8, (l << 8) | c, (int)ts, (int)jj, 0)) return false;
-        ts++;
-    }
+                                              uint32_t jj, uint32_t &pi) {
+    if (g == 1 && !wait_turn(p, turn, l, c, jj)) return false;
     if (!issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, c, jj, pi)) return false;
     pi++;
-    if (g == 0 && both) mbar_arrive(turn);
+    if (g == 0) mbar_arrive(&turn[jj & 1]);
     return true;
 }
 
@@ -515,7 +519,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
     uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
-    uint64_t *const turn = bars + 11;
+    uint64_t *const turn = bars + 16;  // [2], by chunk parity
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -554,7 +558,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
             mbar_init(&p_empty[s], kBM);
         }
         mbar_init(t_ready, kThreadsTc);
-        mbar_init(turn, 1);
+        mbar_init(&turn[0], 1);
+        mbar_init(&turn[1], 1);
         mbar_init(bars + 12, kBM);  // tail exchange: full, empty
         mbar_init(bars + 13, kBM);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -582,29 +587,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
 
     // j: chunks seen consumed; pu / pi: partials of this group drained / issued;
     // tb: T hand-overs between layers seen
-    // ts: chunks of group 0 seen issued (group 1's issuer)
     // xt: tail exchanges seen
-    uint32_t j = 0, pu = 0, pi = 0, tb = 0, ts = 0, xt = 0;
+    uint32_t j = 0, pu = 0, pi = 0, tb = 0, xt = 0;
     bool ok = true;
     float acc[128];
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         for (int l = 0; l < nl && ok; l++) {
             const int nch = p.L[l].nch, Np = p.L[l].Np;
             const bool has_half = 128 * g < Np;
-            const bool both = Np > 128;  // the halves take turns in the tensor pipe
             if (l == 0) {  // the input layer: chunks 0 and 1 from global memory
                 if (halves) {
                     stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 0, j);
                     if (nch > 1) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 1, j + 1);
                 }
                 if (has_half && issuer)
-                    ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi,
-                                       ts, both);
+                    ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi);
             } else if (g == 1 && has_half && issuer) {
                 // group 0 staged chunks 0 and 1 from its registers and issued chunk 0 at
                 // the previous layer's end; group 1's half of chunk 0 follows it
-                ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi, ts,
-                                   both);
+                ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi);
             }
             ok = __all_sync(0xffffffffu, ok);
             {  // while chunk 0 computes: the accumulators start at the bias (zero beyond Np)
@@ -648,12 +649,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                     // the next chunk's MMAs go in before this thread stages anything
                     if (issuer && c + 1 < nch)
                         ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l,
-                                           c + 1, jj + 1, pi, ts, both);
+                                           c + 1, jj + 1, pi);
                     ok = __all_sync(0xffffffffu, ok);
                     if (!ok) break;
                 } else if (issuer) {
-                    umma_commit(&a_empty[s]);  // a group without columns in this layer releases the stage at once
+                    // a group without columns in this layer releases the stage at once (group
+                    // 1 after its turn, which keeps the turn phases in step)
+                    ok = g == 0 || wait_turn(p, turn, l, c, jj);
+                    umma_commit(&a_empty[s]);
                 }
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
                 if (c == 0 && l > 0) {  // T of the previous layer: both halves written (before chunk 2 is staged)
                     ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, l, (int)tb, (int)j, slot));
                     tb++;
@@ -714,7 +720,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
                 stage_from_regs<0>(a0, a_full, r, warp, acc, j);
                 if (issuer)
                     ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, 0, nl1, 0, j,
-                                       pi, ts, p.L[nl1].Np > 128);
+                                       pi);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
 #pragma unroll
