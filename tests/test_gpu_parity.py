@@ -119,18 +119,21 @@ def test_fp64_entry_point(tmp_path):
     assert np.array_equal(o64.T.astype(np.float32), o32)
 
 
-def test_multi_gpu_split_matches(tmp_path):
+@pytest.mark.parametrize("name", ["lstm", "wide_mlp", "cnn"])
+def test_multi_gpu_split_matches(name, tmp_path):
+    """rosenna_use_model_f32 split over the visible GPUs (contiguous sample
+    ranges, weights and tensor maps per device) matches the oracle."""
     count = torch.cuda.device_count()
     if count < 2:
         pytest.skip("one GPU visible")
     api.set_devices(list(range(min(count, 4))))
-    workloads.write_model("lstm", str(tmp_path))
+    workloads.write_model(name, str(tmp_path))
     api.initialize(str(tmp_path))
     n = 10007
-    ins = workloads.make_inputs("lstm", n, seed_offset=5)
+    ins = workloads.make_inputs(name, n, seed_offset=5)
     out = api.use_model_rows(ins)[0]
-    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
-    assert_close(out, ref.reshape(out.shape), "lstm multi-gpu")
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+    assert_close(out, ref.reshape(out.shape), f"{name} multi-gpu")
 
 
 @pytest.mark.parametrize("path", ["tc", "tc_notail", "ffma"])
