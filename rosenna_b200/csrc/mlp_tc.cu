@@ -781,12 +781,329 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     }
 }
 
+// ============================================================================
+// LSTM layer on the tensor cores.  The chunk stream of a tile is T steps of
+// nch = nx + nh K-chunks: x_t (from global memory) then h_{t-1} (from TMEM T,
+// columns 0..Hh-1, written by the cell update of the step before).  Roles,
+// rings, 3xTF32 partials, turn order and bounded waits are those of
+// mlp_tc_kernel; the "layer end" is the cell update: each thread holds the
+// gates of its row for its group's 32 units (columns 4u+q), keeps c in TMEM T
+// (columns 128+32g+u) and writes h to T and, when asked, to y.  The next step's
+// x chunks are staged and its first chunk issued before the cell update, so
+// those MMAs overlap it.
+// ============================================================================
+
+// Stages the K halves in `halves` of chunk q of step s (tile t) into A slot j&1:
+// q < nx from x (feature k = 32q + 16h + e, row s + T*k), else from T (h).
+__device__ __forceinline__ void lstm_stage(const TcLstmArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base,
+                                           int r, int halves, int t, int s, int q, uint32_t j) {
+    uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
+#pragma unroll 1
+    for (int h = 0; h < 2; h++) {
+        if (!(halves & (1 << h))) continue;
+        float v[16];
+        if (q < p.nx) {
+            const long long row = (long long)t * kBM + r;
+            const bool valid = row < p.n;
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                const int k = q * kKC + 16 * h + e;
+                v[e] = (valid && k < p.I) ? __ldg(p.x + (long long)(s + (long long)p.T * k) * p.ld_x + row) : 0.f;
+            }
+        } else {
+            tmem_ld16(lane_base + kTCol + (uint32_t)((q - p.nx) * kKC + 16 * h), v);
+        }
+        put_a16(ahi, ahi + kATile, r, 16 * h, v);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    mbar_arrive(&a_full[j & 1]);
+}
+
+__device__ __forceinline__ void lstm_load_b(const TcLstmArgs &p, uint8_t *b0, uint64_t *b_full, int q, uint32_t j) {
+    const int s = j & 1;
+    mbar_arrive_expect_tx(&b_full[s], 2u * (uint32_t)p.Np * 128u);
+    tma_load_2d(b0 + s * 2 * kBTile, &p.map, &b_full[s], q * kKC, 0);
+    tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.map, &b_full[s], q * kKC, p.Np);
+}
+
+// MMAs of half g for chunk jj (chunk q of its step), as issue_chunk / issue_in_turn.
+__device__ __forceinline__ bool lstm_issue(const TcLstmArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
+                                           uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full, uint64_t *p_empty,
+                                           uint64_t *turn, uint32_t tmem, int g, int q, uint32_t jj, uint32_t &pi) {
+    const int s = jj & 1;
+    if (g == 1 && !mbar_wait(&turn[jj & 1], (jj >> 1) & 1, p.err, 8, q, (int)jj, 0, 0)) return false;
+    if (!mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, q, (int)jj, g, 0)) return false;
+    if (!mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, q, (int)jj, g, 0)) return false;
+    if (!mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, q, (int)pi, (int)jj, 0)) return false;
+    tc_fence_after();
+    const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
+    const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
+    const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;
+    const uint64_t bh = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile)) + boff;
+    const uint64_t bl = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile + kBTile)) + boff;
+    const uint32_t idesc = idesc_tf32(min(128, p.Np - 128 * g));
+    const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
+#pragma unroll
+    for (int kk = 0; kk < kKC / 8; kk++) {
+        const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+        umma_tf32(d, al + adv, bh + adv, idesc, kk);
+        umma_tf32(d, ah + adv, bl + adv, idesc, 1);
+    }
+#pragma unroll
+    for (int kk = 0; kk < kKC / 8; kk++) {
+        const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+        umma_tf32(d, ah + adv, bh + adv, idesc, 1);
+    }
+    umma_commit(&p_full[g]);
+    umma_commit(&a_empty[s]);
+    pi++;
+    if (g == 0) mbar_arrive(&turn[jj & 1]);
+    return true;
+}
+
+__global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_constant__ TcLstmArgs p) {
+    extern __shared__ uint8_t sm_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *const b0 = base;
+    uint8_t *const a0 = base + kSmemB;
+    float *const sbias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
+    uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
+    uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
+    uint64_t *const turn = bars + 16;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = warp >> 2, quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const bool issuer = lane == 0 && (warp == 0 || warp == 5);
+    const int halves = (warp == 0 || warp == 5) ? 0 : (warp == 1 || warp == 4) ? 3 : 1 << g;
+    const bool loader = warp == 2 && lane == 0;
+    const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;
+    const int nch = p.nx + p.nh, T = p.T;
+    const int ntiles = (int)((p.n + kBM - 1) / kBM);
+    const bool has_half = 128 * g < p.Np;
+    // chunks of this CTA: its tiles x T steps x nch
+    const long long my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const long long total = my_tiles * T * nch;
+
+    for (int i = tid; i < kNMax; i += kThreadsTc) sbias[i] = i < p.Np ? p.arena[p.b_off + i] : 0.f;
+    if (tid == 0) {
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&a_full[s], kStagers);
+            mbar_init(&a_empty[s], 2);
+            mbar_init(&p_full[s], 1);
+            mbar_init(&p_empty[s], kBM);
+            mbar_init(&turn[s], 1);
+        }
+        mbar_init(t_ready, kThreadsTc);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+
+    uint32_t b_issued = 0, b_done = 0;
+    if (loader) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&p.map) : "memory");
+        for (long long q = 0; q < 2 && q < total; q++) lstm_load_b(p, b0, b_full, (int)(q % nch), b_issued++);
+    }
+
+    uint32_t j = 0, pu = 0, pi = 0, tb = 0;
+    bool ok = true;
+    float acc[128];
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const long long row = (long long)t * kBM + r;
+        const bool valid = row < p.n;
+        // the initial state: h0 into T columns 32g.., c0 into T columns 128+32g..
+        if (has_half) {
+#pragma unroll
+            for (int hf = 0; hf < 2; hf++) {
+                float hv[16], cv[16];
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const int unit = 32 * g + 16 * hf + e;
+                    float h0 = 0.f, c0 = 0.f;
+                    if (unit < p.H && valid) {
+                        h0 = p.h0 ? p.h0[(long long)unit * p.ld_h0 + row]
+                                  : (p.h0_const >= 0 ? p.arena[p.h0_const + unit] : 0.f);
+                        c0 = p.c0 ? p.c0[(long long)unit * p.ld_c0 + row]
+                                  : (p.c0_const >= 0 ? p.arena[p.c0_const + unit] : 0.f);
+                    }
+                    hv[e] = h0;
+                    cv[e] = c0;
+                }
+                tmem_st16(lane_base + kTCol + (uint32_t)(32 * g + 16 * hf), hv);
+                tmem_st16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
+            }
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(t_ready);
+        ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, 0, (int)tb, (int)j, slot));
+        tb++;
+        tc_fence_after();
+        if (!ok) break;
+        // step 0: chunks 0 and 1 staged here, chunk 0 issued; later steps had
+        // theirs staged (and chunk 0 issued) during the step before
+        if (halves) {
+            lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 0, j);
+            if (nch > 1) lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 1, j + 1);
+        }
+        if (has_half && issuer) ok = lstm_issue(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, 0, j, pi);
+        ok = __all_sync(0xffffffffu, ok);
+        for (int st = 0; st < T && ok; st++) {
+            if (has_half) {
+                const uint32_t b_addr = smem_u32(sbias + 128 * g);
+#pragma unroll
+                for (int q = 0; q < 32; q++)
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
+                                 : "r"(b_addr + 16u * q));
+            }
+            for (int c = 0; c < nch && ok; c++) {
+                const uint32_t jj = j + (uint32_t)c;
+                const int s = jj & 1;
+                if (has_half) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (st << 8) | c, (int)pu,
+                                                           (int)jj, slot));
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int q0 = 0; q0 < 8; q0 += 4) {
+                        if (128 * g + 16 * q0 < p.Np) {
+                            uint32_t v[4][16];
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (128 * g + 16 * (q0 + u) < p.Np)
+                                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (128 * g + 16 * (q0 + u) < p.Np) {
+#pragma unroll
+                                    for (int e = 0; e < 16; e += 2)
+                                        add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e], v[u][e + 1]);
+                                }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&p_empty[g]);
+                    pu++;
+                    // the next chunk goes in at once: this step's, or the next step's first (x)
+                    if (issuer && (c + 1 < nch || st + 1 < T))
+                        ok = lstm_issue(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g,
+                                        c + 1 < nch ? c + 1 : 0, jj + 1, pi);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) break;
+                } else if (issuer) {
+                    ok = mbar_wait(&turn[jj & 1], (jj >> 1) & 1, p.err, 8, c, (int)jj, 0, 0);
+                    umma_commit(&a_empty[s]);
+                }
+                ok = __all_sync(0xffffffffu, ok &&
+                                mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (st << 8) | c, (int)jj, (int)pu, slot));
+                if (!ok) break;
+                if (loader) {
+                    b_done = jj + 1;
+                    const long long q2 = (long long)jj + 2 - 0;  // chunk index of this CTA's stream
+                    if (q2 < total) lstm_load_b(p, b0, b_full, (int)(q2 % nch), b_issued++);
+                }
+                // stage chunk c+2: of this step, or an x chunk of the next step (an h
+                // chunk of the next step waits for this step's cell update)
+                if (halves) {
+                    const int q2 = c + 2;
+                    if (q2 < nch) lstm_stage(p, a0, a_full, lane_base, r, halves, t, st, q2, jj + 2);
+                    else if (st + 1 < T && q2 - nch < p.nx)
+                        lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, q2 - nch, jj + 2);
+                }
+            }
+            j += (uint32_t)nch;
+            if (!ok) break;
+            // cell update (layers.f90 lstm_cell): gates of unit u at acc[4u..4u+3]
+            if (has_half) {
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    float cv[16], hv[16];
+                    tmem_ld16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const int u = 16 * hf + e;
+                        const float ig = tc_act<3>(acc[4 * u]), fg = tc_act<3>(acc[4 * u + 1]);
+                        const float gg = tc_act<2>(acc[4 * u + 2]), og = tc_act<3>(acc[4 * u + 3]);
+                        cv[e] = fg * cv[e] + ig * gg;
+                        hv[e] = og * tc_act<2>(cv[e]);
+                    }
+                    tmem_st16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
+                    tmem_st16(lane_base + kTCol + (uint32_t)(32 * g + 16 * hf), hv);
+                    if (valid) {
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            const int unit = 32 * g + 16 * hf + e;
+                            if (unit < p.H) {
+                                if (p.y) p.y[(long long)(st + (long long)T * unit) * p.ld_y + row] = hv[e];
+                                if (st + 1 == T) {
+                                    if (p.hn) p.hn[(long long)unit * p.ld_hn + row] = hv[e];
+                                    if (p.cn) p.cn[(long long)unit * p.ld_cn + row] = cv[e];
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            // h_t in T for the next step (both groups' units feed both groups' MMAs)
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(t_ready);
+            ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, st, (int)tb, (int)j, slot));
+            tb++;
+            tc_fence_after();
+            if (!ok) break;
+            // the next step's chunk 1 when it is an h chunk (nx == 1)
+            if (halves && st + 1 < T && nch > 1 && p.nx == 1)
+                lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, 1, j + 1);
+        }
+    }
+    if (issuer) {
+        umma_commit(&p_full[g]);
+        for (uint32_t k = pu; k <= pi; k++) mbar_wait(&p_full[g], k & 1, p.err, 0);
+    }
+    if (loader)
+        for (uint32_t k = b_done; k < b_issued; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
 }  // namespace
 
 size_t mlp_tc_smem_bytes() { return 1024 + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX + kSmemBars; }
 
 cudaError_t mlp_tc_configure() {
-    return cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());
+    cudaError_t e =
+        cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(lstm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());
+}
+
+cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st) {
+    const long long tiles = (a.n + kBM - 1) / kBM;
+    const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+    if (grid <= 0) return cudaSuccess;
+    lstm_tc_kernel<<<grid, kThreadsTc, mlp_tc_smem_bytes(), st>>>(a);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st) {

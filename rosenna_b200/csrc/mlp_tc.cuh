@@ -36,9 +36,35 @@ struct TcArgs {
     long long tail_w_off, tail_b_off;
 };
 
+// One LSTM layer (fLibrary/layers.f90 lstm / lstm_cell) on the tensor cores,
+// for 4H <= 256: every time step is a 128-sample x (4H gates) x (Ix + Hh)
+// product of [x_t | h_{t-1}] with the packed [2*Np][Kp] block (rows n = 4j+q:
+// gate q of unit j, hi then lo), followed by the cell update in registers.
+struct TcLstmArgs {
+    CUtensorMap map;  // over the block, box {32, Np}
+    const float *arena;
+    long long b_off, h0_const, c0_const;  // gate bias [Np]; per-unit constant state or -1
+    const float *x;
+    long long ld_x;  // row t + T*i
+    const float *h0;
+    long long ld_h0;
+    const float *c0;
+    long long ld_c0;
+    float *y;
+    long long ld_y;  // row t + T*j
+    float *hn;
+    long long ld_hn;
+    float *cn;
+    long long ld_cn;
+    long long n;
+    int *err;
+    int T, I, H, Np, nx, nh;  // nx / nh: K chunks of 32 of the x / h parts
+};
+
 size_t mlp_tc_smem_bytes();
 cudaError_t mlp_tc_configure();
 cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st);
+cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
 
 // Encodes the TMA map of one layer block at `block` (device pointer).
 // Returns false (with *why set) when the driver entry point or encode fails.

@@ -393,6 +393,30 @@ Status Builder::op_lstm(const PyVal &e) {  // modelCreator.fpp:92-100, layers.f9
         }
     s.w_off = put(wt.data(), wt.size());
     s.b_off = put(bias.data(), bias.size());
+    if (4 * H <= 256) {  // tensor-core block: tf32 hi rows, then the rounded remainders
+        const int Np = (int)round_up(4 * H, 16), Ix = (int)round_up(I, 32), Hh = (int)round_up(H, 32);
+        const int Kp = Ix + Hh;
+        std::vector<float> blk((size_t)2 * Np * Kp, 0.f), tb((size_t)Np, 0.f);
+        for (int j = 0; j < H; j++)
+            for (int q = 0; q < 4; q++) {
+                const int n = 4 * j + q, r = q * H + j;
+                for (int k = 0; k < I + H; k++) {
+                    const double wv = k < I ? L.wih.v[(size_t)r + (size_t)4 * H * k]
+                                            : L.whh.v[(size_t)r + (size_t)4 * H * (k - I)];
+                    const int col = k < I ? k : Ix + (k - I);
+                    const float w = (float)wv, hi = tf32_round(w);
+                    blk[(size_t)n * Kp + col] = hi;
+                    blk[(size_t)(Np + n) * Kp + col] = tf32_round(w - hi);
+                }
+                tb[(size_t)n] = (float)(L.bih.v[(size_t)r] + L.bhh.v[(size_t)r]);
+            }
+        s.lstm_tc_w_off = put(blk.data(), blk.size());
+        s.lstm_tc_b_off = put(tb.data(), tb.size());
+        s.lstm_tc_Np = Np;
+        s.lstm_tc_Kp = Kp;
+        s.lstm_tc_nx = Ix / 32;
+        s.lstm_tc_nh = Hh / 32;
+    }
     s.y = new_buf((int64_t)T * H);
     s.hn = new_buf(H);
     s.cn = new_buf(H);
@@ -712,7 +736,7 @@ std::string Plan::describe() const {
                 o << "]\n";
                 break;
             case Step::LSTM:
-                o << "lstm b" << s.in << " T=" << s.T << " I=" << s.I << " H=" << s.H << " h0=b" << s.h0 << " c0=b"
+                o << (s.tc ? "lstm_tc b" : "lstm b") << s.in << " T=" << s.T << " I=" << s.I << " H=" << s.H << " h0=b" << s.h0 << " c0=b"
                   << s.c0 << " -> y=b" << s.y << " hn=b" << s.hn << " cn=b" << s.cn << "\n";
                 break;
             case Step::CONV:

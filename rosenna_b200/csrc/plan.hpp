@@ -44,6 +44,10 @@ struct Step {
     int h0 = -1, c0 = -1;              // buffers of the initial state, or -1
     int64_t h0_const = -1, c0_const = -1;  // arena offsets of a per-unit constant initial state
     int y = -1, hn = -1, cn = -1;      // output buffers (-1 when nothing reads them)
+    // tensor-core copy of an LSTM layer with 4H <= 256: [2*Np][Kp] block, rows
+    // n = 4j+q (gate q of unit j) hi then lo, columns [x (nx chunks of 32) | h (nh)]
+    int64_t lstm_tc_w_off = -1, lstm_tc_b_off = -1;
+    int lstm_tc_Np = 0, lstm_tc_Kp = 0, lstm_tc_nx = 0, lstm_tc_nh = 0;
 
     // CONV (+ReLU) (+pool); conv == false means pooling only
     bool conv = true, relu = false;

@@ -47,6 +47,7 @@ struct Device {
     int *err = nullptr;       // tensor-core kernel status word (0 = ok)
     int *err_host = nullptr;  // pinned copy, refreshed after each tensor-core launch
     std::vector<TcArgs> tc_args;  // per plan step (tensor-core MLP steps only)
+    std::vector<TcLstmArgs> lstm_args;  // per plan step (tensor-core LSTM steps only)
     Slot slots[kSlots];
 };
 
@@ -210,6 +211,25 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 break;
             }
             case Step::LSTM: {
+                if (s.tc) {
+                    TcLstmArgs a = d.lstm_args[si];
+                    a.x = ptr[(size_t)s.in];
+                    a.ld_x = ld[(size_t)s.in];
+                    a.h0 = nullptr;
+                    a.c0 = nullptr;
+                    a.y = a.hn = a.cn = nullptr;
+                    if (s.h0 >= 0) { a.h0 = ptr[(size_t)s.h0]; a.ld_h0 = ld[(size_t)s.h0]; }
+                    if (s.c0 >= 0) { a.c0 = ptr[(size_t)s.c0]; a.ld_c0 = ld[(size_t)s.c0]; }
+                    if (s.y >= 0) { a.y = ptr[(size_t)s.y]; a.ld_y = ld[(size_t)s.y]; }
+                    if (s.hn >= 0) { a.hn = ptr[(size_t)s.hn]; a.ld_hn = ld[(size_t)s.hn]; }
+                    if (s.cn >= 0) { a.cn = ptr[(size_t)s.cn]; a.ld_cn = ld[(size_t)s.cn]; }
+                    a.n = cnt;
+                    e = launch_lstm_tc(a, d.num_sms, stream);
+                    launches++;
+                    if (e == cudaSuccess)
+                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    break;
+                }
                 LstmArgs a{};
                 a.arena = arena;
                 a.w_off = s.w_off;
@@ -414,6 +434,14 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         }
         s.tc = eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 128);
     }
+    // tensor-core LSTM for 128 < 4H <= 256, both column halves busy (with 4H <= 128
+    // one half idles and the per-step chain is latency-bound: the FFMA kernel is
+    // faster); ROSENNA_LSTM_PATH=ffma / =tc force either kernel
+    const char *lpath = getenv("ROSENNA_LSTM_PATH");
+    const std::string lstm_path = lpath ? lpath : "";
+    for (auto &s : P.steps)
+        if (s.kind == Step::LSTM)
+            s.tc = lstm_path != "ffma" && s.lstm_tc_w_off >= 0 && (lstm_path == "tc" || 4 * s.H > 128);
     g_ctx.is_io_in.assign(P.buf_rows.size(), false);
     g_ctx.is_io_out.assign(P.buf_rows.size(), false);
     for (auto &io : P.inputs) g_ctx.is_io_in[(size_t)io.buf] = true;
@@ -446,6 +474,26 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         CUDA_TRY(cudaMallocHost(&d->err_host, 64 * sizeof(int)));
         std::memset(d->err_host, 0, 64 * sizeof(int));
         d->tc_args.assign(P.steps.size(), TcArgs{});
+        d->lstm_args.assign(P.steps.size(), TcLstmArgs{});
+        for (size_t si = 0; si < P.steps.size(); si++) {
+            const Step &s = P.steps[si];
+            if (s.kind != Step::LSTM || !s.tc) continue;
+            TcLstmArgs &a = d->lstm_args[si];
+            a.arena = d->arena;
+            a.err = d->err;
+            a.b_off = s.lstm_tc_b_off;
+            a.h0_const = s.h0_const;
+            a.c0_const = s.c0_const;
+            a.T = s.T;
+            a.I = s.I;
+            a.H = s.H;
+            a.Np = s.lstm_tc_Np;
+            a.nx = s.lstm_tc_nx;
+            a.nh = s.lstm_tc_nh;
+            const char *why = "";
+            if (!mlp_tc_encode_map(&a.map, d->arena + s.lstm_tc_w_off, s.lstm_tc_Kp, s.lstm_tc_Np, &why))
+                return Status::Err(ROSENNA_ERR_CUDA, why);
+        }
         for (size_t si = 0; si < P.steps.size(); si++) {
             const Step &s = P.steps[si];
             if (!s.tc) continue;

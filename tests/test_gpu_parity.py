@@ -155,6 +155,22 @@ def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
         assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
 
 
+@pytest.mark.parametrize("path", ["tc", "ffma"])
+@pytest.mark.parametrize("name", ["lstm", "lstm2"])
+def test_lstm_kernel_paths(name, path, tmp_path, monkeypatch):
+    """Both LSTM kernels (tcgen05 3xTF32 and FFMA) on both LSTM workloads."""
+    monkeypatch.setenv("ROSENNA_LSTM_PATH", path)
+    workloads.write_model(name, str(tmp_path))
+    api.initialize(str(tmp_path))
+    desc = api.plan_description()
+    assert ("lstm_tc" in desc) == (path == "tc"), desc
+    for n in (1, 129, 1000, 4099):
+        ins = workloads.make_inputs(name, n, seed_offset=3 + n)
+        out = api.use_model_rows(ins)[0]
+        ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+        assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
+
+
 @pytest.mark.parametrize("conv_path", ["tiled", "direct"])
 def test_cnn_conv_paths(conv_path, tmp_path):
     """The tiled conv+pool kernel and the per-element one on the CNN workload and
