@@ -793,16 +793,51 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
 // those MMAs overlap it.
 // ============================================================================
 
+// Shared memory of lstm_tc_kernel: the B and A rings of mlp_tc_kernel, the gate
+// bias, and a buffer for the next step's x (up to two chunks, [k][128 rows] fp32)
+// filled by cp.async one step ahead.
+constexpr uint32_t kLstmBias = 1024, kLstmXBuf = 2 * kKC * kBM * 4;
+constexpr int kLstmMaxNxPrefetch = 2;
+size_t lstm_tc_smem() { return 1024 + kSmemB + kSmemA + kLstmBias + kLstmXBuf + kSmemBars; }
+
+__device__ __forceinline__ void cp_async4_zfill(float *dst, const float *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+
+// Copies (cp.async) this thread's row of the x chunks of step s into the buffer.
+__device__ __forceinline__ void lstm_prefetch_x(const TcLstmArgs &p, float *xbuf, int r, int halves, int t, int s) {
+    const long long row = (long long)t * kBM + r;
+    const bool valid = row < p.n;
+    for (int q = 0; q < p.nx; q++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            if (!(halves & (1 << h))) continue;
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                const int k = q * kKC + 16 * h + e;
+                const bool ok = valid && k < p.I;
+                cp_async4_zfill(xbuf + (size_t)k * kBM + r, ok ? p.x + (long long)(s + (long long)p.T * k) * p.ld_x + row : p.x,
+                                ok);
+            }
+        }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // Stages the K halves in `halves` of chunk q of step s (tile t) into A slot j&1:
 // q < nx from x (feature k = 32q + 16h + e, row s + T*k), else from T (h).
 __device__ __forceinline__ void lstm_stage(const TcLstmArgs &p, uint8_t *a0, uint64_t *a_full, uint32_t lane_base,
-                                           int r, int halves, int t, int s, int q, uint32_t j) {
+                                           int r, int halves, int t, int s, int q, uint32_t j, const float *xbuf) {
     uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
+    if (xbuf && q < p.nx) asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll 1
     for (int h = 0; h < 2; h++) {
         if (!(halves & (1 << h))) continue;
         float v[16];
-        if (q < p.nx) {
+        if (xbuf && q < p.nx) {  // prefetched by this thread
+#pragma unroll
+            for (int e = 0; e < 16; e++) v[e] = xbuf[(size_t)(q * kKC + 16 * h + e) * kBM + r];
+        } else if (q < p.nx) {
             const long long row = (long long)t * kBM + r;
             const bool valid = row < p.n;
 #pragma unroll
@@ -868,7 +903,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
     uint8_t *const b0 = base;
     uint8_t *const a0 = base + kSmemB;
     float *const sbias = reinterpret_cast<float *>(base + kSmemB + kSmemA);
-    uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
+    float *const xbuf_all = reinterpret_cast<float *>(base + kSmemB + kSmemA + kLstmBias);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kLstmBias + kLstmXBuf);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
     uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
     uint64_t *const turn = bars + 16;
@@ -884,11 +920,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
     const int nch = p.nx + p.nh, T = p.T;
     const int ntiles = (int)((p.n + kBM - 1) / kBM);
     const bool has_half = 128 * g < p.Np;
+    // the next step's x through the prefetch buffer (x parts of up to two chunks)
+    float *const xbuf = (halves && p.nx <= kLstmMaxNxPrefetch) ? xbuf_all : nullptr;
     // chunks of this CTA: its tiles x T steps x nch
     const long long my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const long long total = my_tiles * T * nch;
 
     for (int i = tid; i < kNMax; i += kThreadsTc) sbias[i] = i < p.Np ? p.arena[p.b_off + i] : 0.f;
+    static_assert(kNMax * 4 <= kLstmBias, "bias area");
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
@@ -956,12 +995,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
         // step 0: chunks 0 and 1 staged here, chunk 0 issued; later steps had
         // theirs staged (and chunk 0 issued) during the step before
         if (halves) {
-            lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 0, j);
-            if (nch > 1) lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 1, j + 1);
+            lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 0, j, nullptr);
+            if (nch > 1) lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 1, j + 1, nullptr);
         }
         if (has_half && issuer) ok = lstm_issue(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, 0, j, pi);
         ok = __all_sync(0xffffffffu, ok);
         for (int st = 0; st < T && ok; st++) {
+            // x of the next step: its chunks are staged at this step's last iterations
+            if (xbuf && st + 1 < T) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
             if (has_half) {
                 const uint32_t b_addr = smem_u32(sbias + 128 * g);
 #pragma unroll
@@ -1021,9 +1062,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
                 // chunk of the next step waits for this step's cell update)
                 if (halves) {
                     const int q2 = c + 2;
-                    if (q2 < nch) lstm_stage(p, a0, a_full, lane_base, r, halves, t, st, q2, jj + 2);
+                    if (q2 < nch) lstm_stage(p, a0, a_full, lane_base, r, halves, t, st, q2, jj + 2, xbuf);
                     else if (st + 1 < T && q2 - nch < p.nx)
-                        lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, q2 - nch, jj + 2);
+                        lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, q2 - nch, jj + 2, xbuf);
                 }
             }
             j += (uint32_t)nch;
@@ -1069,7 +1110,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
             if (!ok) break;
             // the next step's chunk 1 when it is an h chunk (nx == 1)
             if (halves && st + 1 < T && nch > 1 && p.nx == 1)
-                lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, 1, j + 1);
+                lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, 1, j + 1, xbuf);
         }
     }
     if (issuer) {
@@ -1095,14 +1136,14 @@ cudaError_t mlp_tc_configure() {
     cudaError_t e =
         cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(lstm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());
+    return cudaFuncSetAttribute(lstm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lstm_tc_smem());
 }
 
 cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st) {
     const long long tiles = (a.n + kBM - 1) / kBM;
     const int grid = (int)(tiles < num_sms ? tiles : num_sms);
     if (grid <= 0) return cudaSuccess;
-    lstm_tc_kernel<<<grid, kThreadsTc, mlp_tc_smem_bytes(), st>>>(a);
+    lstm_tc_kernel<<<grid, kThreadsTc, lstm_tc_smem(), st>>>(a);
     return cudaGetLastError();
 }
 
