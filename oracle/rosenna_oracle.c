@@ -8,7 +8,7 @@
  * It is an fp64 restatement of roseNNa's Fortran library, written in C because
  * no Fortran compiler exists in this image (the reference cannot be built):
  *   - the weight reader             fLibrary/reader.f90:38-290
- *   - the layers                    fLibrary/layers.f90:11-310
+ *   - the layers                    fLibrary/layers.f90:11-375
  *   - the activations               fLibrary/activation_funcs.f90:7-64
  *   - the generated use_model body  fLibrary/modelCreator.fpp:42-171
  * The generated use_model is a straight-line Fortran program that fypp expands
@@ -655,6 +655,78 @@ static int pool_layer(Arr *inp, int ks, const int *pads, const int *strides, int
     return 0;
 }
 
+/* broadc, fLibrary/layers.f90:351-375: SPREAD the 4-D adder along each
+ * (dim, copies) pair of spreadInfo in turn, each time RESHAPEd (column-major,
+ * the first elements taken, as Fortran's RESHAPE does) to trueShape(:dim)
+ * followed by the adder's ORIGINAL trailing dims (`inter` is never updated);
+ * the last pair RESHAPEs to trueShape. */
+static int broadc(const Arr *inp, const int *trueShape, const int *spread, int npairs, Arr *out) {
+    Arr cur = arr_copy(inp);
+    for (int i = 0; i < npairs; i++) {
+        const int d = spread[2 * i], n = spread[2 * i + 1];
+        if (d < 1 || d > 4 || n < 1) { arr_free(&cur); return -1; }
+        int64_t P = 1, rest = 1;
+        for (int k = 0; k < d - 1; k++) P *= cur.d[k];
+        for (int k = d - 1; k < 4; k++) rest *= cur.d[k];
+        /* SPREAD(cur, d, n): sp(a, k, b) = cur(a, b), a over dims < d, b over dims >= d */
+        double *sp = (double *)malloc(sizeof(double) * (size_t)(P * n * rest > 0 ? P * n * rest : 1));
+        for (int64_t b = 0; b < rest; b++)
+            for (int k = 0; k < n; k++)
+                for (int64_t a = 0; a < P; a++) sp[a + P * (k + (int64_t)n * b)] = cur.v[a + P * b];
+        int shape[4];
+        if (i != npairs - 1) {
+            for (int k = 0; k < 4; k++) shape[k] = k < d ? trueShape[k] : inp->d[k];
+        } else {
+            for (int k = 0; k < 4; k++) shape[k] = trueShape[k];
+        }
+        Arr nx = arr_new(4, shape);
+        int64_t need = arr_numel(&nx);
+        if (need > P * n * rest) { free(sp); arr_free(&nx); arr_free(&cur); return -1; }
+        memcpy(nx.v, sp, sizeof(double) * (size_t)need);
+        free(sp);
+        arr_free(&cur);
+        cur = nx;
+    }
+    *out = cur;
+    return 0;
+}
+
+/* matmul2D / matmul3D / matmul4D, fLibrary/layers.f90:25-60: inp1 = inp1 . inp2
+ * over the last two dims, per index of the leading dims of inp1 (inp2 indexed
+ * by the same leading indices). */
+static int matmul_nd(Arr *inp1, const Arr *inp2, int rank) {
+    if (rank < 2 || rank > 4 || inp1->rank != rank || inp2->rank != rank) return -1;
+    const int P = inp1->d[rank - 2], K = inp1->d[rank - 1], M = inp2->d[rank - 1];
+    if (inp2->d[rank - 2] != K) return -2;
+    int lead1[2] = {1, 1}, lead2[2] = {1, 1};
+    for (int k = 0; k < rank - 2; k++) {
+        lead1[k] = inp1->d[k];
+        lead2[k] = inp2->d[k];
+        if (lead2[k] < lead1[k]) return -2;
+    }
+    int d[MAXR];
+    for (int k = 0; k < rank; k++) d[k] = inp1->d[k];
+    d[rank - 1] = M;
+    Arr o = arr_new(rank, d);
+    /* element (i, j, p, q) of a rank-4 array with dims (D1, D2, D3, D4) sits at
+     * i + D1*(j + D2*(p + D3*q)); leading dims first */
+    const int64_t L1 = (int64_t)lead1[0] * lead1[1], L2 = (int64_t)lead2[0] * lead2[1];
+    for (int j = 0; j < lead1[1]; j++)
+        for (int i = 0; i < lead1[0]; i++) {
+            const int64_t o1 = i + (int64_t)lead1[0] * j, o2 = i + (int64_t)lead2[0] * j;
+            for (int p = 0; p < P; p++)
+                for (int q = 0; q < M; q++) {
+                    double acc = 0;
+                    for (int k = 0; k < K; k++)
+                        acc += inp1->v[o1 + L1 * (p + (int64_t)P * k)] * inp2->v[o2 + L2 * (k + (int64_t)K * q)];
+                    o.v[o1 + L1 * (p + (int64_t)P * q)] = acc;
+                }
+        }
+    arr_free(inp1);
+    *inp1 = o;
+    return 0;
+}
+
 /* --------------------------------------------------------- interpreter */
 
 typedef struct {
@@ -833,6 +905,33 @@ static int run_op(const ro_model *m, Vars *vs, const PV *tup, Counters *cnt, cha
         Arr o = arr_new(nr, ns);
         memcpy(o.v, x->v, sizeof(double) * (size_t)arr_numel(x));
         var_set(vs, on, o);
+    } else if (!strcmp(op, "Add")) { /* modelCreator.fpp:137-144 */
+        Arr *x = var_get(vs, pv_str(pv_at(a1, 0)));
+        int ts[4], sp[2 * MAXR * 2];
+        const int nt = pv_ints(pv_at(a2, 0), ts, 4);
+        const int ns = pv_ints(pv_at(a2, 1), sp, 2 * MAXR * 2);
+        const int rank = (int)pv_int(pv_at(a2, 2));
+        if (!x || cnt->add >= m->nadd || nt != 4 || ns < 0 || (ns & 1) || rank < 1 || rank > 4 || x->rank != rank) {
+            set_err(err, errlen, "Add: bad input or layer");
+            return -1;
+        }
+        const Arr *A = &m->add[cnt->add].adder;
+        Arr b;
+        if (ns == 0) b = arr_copy(A);
+        else if (broadc(A, ts, sp, ns / 2, &b)) { set_err(err, errlen, "Add: broadcast shapes do not fit"); return -1; }
+        /* x = x + RESHAPE(b, trueShape(5-rank:)): the first numel(x) elements, column-major */
+        const int64_t n = arr_numel(x);
+        int64_t tn = 1;
+        for (int k = 4 - rank; k < 4; k++) tn *= ts[k];
+        if (tn != n || arr_numel(&b) < n) { arr_free(&b); set_err(err, errlen, "Add: shape mismatch"); return -1; }
+        for (int64_t i = 0; i < n; i++) x->v[i] += b.v[i];
+        arr_free(&b);
+        cnt->add++;
+    } else if (!strcmp(op, "MatMul")) { /* modelCreator.fpp:146-149 */
+        Arr *x = var_get(vs, pv_str(pv_at(a1, 0)));
+        const Arr *y = var_get(vs, pv_str(pv_at(a1, 1)));
+        const int rank = (int)pv_int(pv_at(a2, 0));
+        if (!x || !y || matmul_nd(x, y, rank)) { set_err(err, errlen, "MatMul: bad operands"); return -1; }
     } else if (!strcmp(op, "Relu") || !strcmp(op, "Tanh") || !strcmp(op, "Sigmoid")) { /* modelCreator.fpp:151-161 */
         Arr *x = var_get(vs, pv_str(pv_at(a1, 0)));
         if (!x) { set_err(err, errlen, "%s: missing input", op); return -1; }

@@ -384,7 +384,7 @@ __device__ __forceinline__ float conv_value(const ConvArgs &p, const float *in, 
 // Semantics are those of conv_pool_kernel below: conv zero padding by skipping,
 // pool-window positions outside the conv output count as 0.
 template <int KS, int PK, int OCB>
-__global__ void __launch_bounds__(256, 2) conv_pool_tile_kernel(const ConvArgs p) {
+__global__ void __launch_bounds__(256, (PK - 1 + KS) > 5 || PK == 3 ? 1 : 2) conv_pool_tile_kernel(const ConvArgs p) {
     extern __shared__ float sw[];
     constexpr int P = PK - 1 + KS;  // input patch side of one pool window
     const int OCp = (p.OC + OCB - 1) / OCB * OCB;
@@ -419,6 +419,44 @@ __global__ void __launch_bounds__(256, 2) conv_pool_tile_kernel(const ConvArgs p
         const float *pin = inner ? in + (long long)p.C * (ih0 + p.Hin * iw0) * p.ld_in : in;
 #pragma unroll 1
         for (int ic = 0; ic < p.C; ic++) {
+            if constexpr (P > 5) {
+                // wide patches stream row by row (P registers instead of P*P):
+                // patch row ar feeds conv row a = ar - kh of every kernel row kh
+#pragma unroll
+                for (int ar = 0; ar < P; ar++) {
+                    float xr[P];
+#pragma unroll
+                    for (int b = 0; b < P; b++) {
+                        const int ih = ih0 + ar, iw = iw0 + b;
+                        xr[b] = inner ? __ldg(pin + (long long)ic * p.ld_in + ar * sa + b * sb)
+                                      : (valid && ih >= 0 && ih < p.Hin && iw >= 0 && iw < p.Win)
+                                            ? __ldg(in + (long long)(ic + p.C * (ih + p.Hin * iw)) * p.ld_in)
+                                            : 0.f;
+                    }
+#pragma unroll
+                    for (int kh = 0; kh < KS; kh++) {
+                        const int a = ar - kh;
+                        if (a < 0 || a >= PK) continue;
+#pragma unroll
+                        for (int kw = 0; kw < KS; kw++) {
+                            const float4 *w4 = reinterpret_cast<const float4 *>(wg + ((ic * KS + kh) * KS + kw) * OCp);
+#pragma unroll
+                            for (int o4 = 0; o4 < OCB / 4; o4++) {
+                                const float4 w = w4[o4];
+#pragma unroll
+                                for (int b = 0; b < PK; b++) {
+                                    const float xv = xr[b + kw];
+                                    acc[a][b][4 * o4 + 0] = fmaf(w.x, xv, acc[a][b][4 * o4 + 0]);
+                                    acc[a][b][4 * o4 + 1] = fmaf(w.y, xv, acc[a][b][4 * o4 + 1]);
+                                    acc[a][b][4 * o4 + 2] = fmaf(w.z, xv, acc[a][b][4 * o4 + 2]);
+                                    acc[a][b][4 * o4 + 3] = fmaf(w.w, xv, acc[a][b][4 * o4 + 3]);
+                                }
+                            }
+                        }
+                    }
+                }
+                continue;
+            }
             float x[P][P];
             if (inner) {
                 const float *q = pin + (long long)ic * p.ld_in;
@@ -516,11 +554,15 @@ __global__ void gather_kernel(const float *in, long long ld_in, float *out, long
     out[r * ld_out + s] = in[src * ld_in + s];
 }
 
-__global__ void act_kernel(const float *in, long long ld_in, float *out, long long ld_out, long long n, int act) {
+// out row r = act(in row r (+ add[r])): standalone activations and the Add of a
+// per-row constant (an ONNX Add whose adder broadcasts over the samples)
+__global__ void act_kernel(const float *in, long long ld_in, float *out, long long ld_out, long long n, int act,
+                           const float *add) {
     const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
     const long long r = blockIdx.y;
-    out[r * ld_out + s] = apply_act(in[r * ld_in + s], act);
+    const float x = in[r * ld_in + s];
+    out[r * ld_out + s] = apply_act(add ? x + add[r] : x, act);
 }
 
 }  // namespace
@@ -609,18 +651,27 @@ static cudaError_t launch_conv_tile(const ConvArgs &a, cudaStream_t st) {
 cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
     const long long outs = (long long)a.OC * a.Hq * a.Wq;
     if (a.n <= 0 || outs <= 0) return cudaSuccess;
-    // the tiled kernel: stride-1 3x3 convolution, no pool or a 2x2 pool window
-    // (weights and bias within the default 48 KB of dynamic shared memory);
-    // ROSENNA_CONV_PATH=direct keeps every convolution on the per-element kernel
+    // the tiled kernel: stride-1 3x3 convolution with no pool or a pool window
+    // of 2 or 3, 5x5 with no pool or a window of 2 (5x5 under a 3-wide window
+    // spills even at 255 registers); weights and bias within the default 48 KB
+    // of dynamic shared memory.  ROSENNA_CONV_PATH=direct keeps every
+    // convolution on the per-element kernel
     static const bool direct_only = [] {
         const char *e = getenv("ROSENNA_CONV_PATH");
         return e && std::string(e) == "direct";
     }();
-    if (!direct_only && a.conv && a.KS == 3 && a.str_h == 1 && a.str_w == 1 && (a.pool == 0 || a.pk == 2) &&
-        ((size_t)a.C * 9 + 1) * ((a.OC + 7) / 8 * 8) * sizeof(float) <= 48 * 1024) {
+    const int pk = a.pool == 0 ? 1 : a.pk;
+    const int ocb = pk == 3 ? 4 : 8;  // 3x3 pooled windows of 8 channels would not fit 128 registers
+    if (!direct_only && a.conv && (a.KS == 3 || a.KS == 5) && a.str_h == 1 && a.str_w == 1 && pk <= (a.KS == 3 ? 3 : 2) &&
+        ((size_t)a.C * a.KS * a.KS + 1) * ((a.OC + ocb - 1) / ocb * ocb) * sizeof(float) <= 48 * 1024) {
         // 8 output channels per item: two CTAs per SM fit (16 per item spills or halves occupancy)
-        if (a.pool == 0) return launch_conv_tile<3, 1, 8>(a, st);
-        return launch_conv_tile<3, 2, 8>(a, st);
+        if (a.KS == 3) {
+            if (pk == 1) return launch_conv_tile<3, 1, 8>(a, st);
+            if (pk == 2) return launch_conv_tile<3, 2, 8>(a, st);
+            return launch_conv_tile<3, 3, 4>(a, st);
+        }
+        if (pk == 1) return launch_conv_tile<5, 1, 8>(a, st);
+        return launch_conv_tile<5, 2, 8>(a, st);
     }
     if (outs > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((a.n + 127) / 128), (unsigned)outs);
@@ -638,11 +689,11 @@ cudaError_t launch_gather(const float *in, long long ld_in, float *out, long lon
 }
 
 cudaError_t launch_act(const float *in, long long ld_in, float *out, long long ld_out, long long rows, long long n,
-                       int act, cudaStream_t st) {
+                       int act, const float *add, cudaStream_t st) {
     if (n <= 0 || rows <= 0) return cudaSuccess;
     if (rows > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((n + 255) / 256), (unsigned)rows);
-    act_kernel<<<grid, 256, 0, st>>>(in, ld_in, out, ld_out, n, act);
+    act_kernel<<<grid, 256, 0, st>>>(in, ld_in, out, ld_out, n, act, add);
     return cudaGetLastError();
 }
 

@@ -66,8 +66,9 @@ cudaError_t launch_lstm(LstmArgs a, int num_sms, cudaStream_t st);
 cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st);
 cudaError_t launch_gather(const float *in, long long ld_in, float *out, long long ld_out, const int *map, long long rows,
                           long long n, cudaStream_t st);
+// add: per-row constant added before the activation, or nullptr
 cudaError_t launch_act(const float *in, long long ld_in, float *out, long long ld_out, long long rows, long long n,
-                       int act, cudaStream_t st);
+                       int act, const float *add, cudaStream_t st);
 
 // Opt the kernels into large dynamic shared memory on the current device.
 cudaError_t configure_kernels();

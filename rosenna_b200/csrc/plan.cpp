@@ -7,6 +7,11 @@
 //   Conv (+ Relu) (+ MaxPool/AveragePool)  -> one fused conv/pool step
 //   Transpose / Squeeze / Reshape          -> nothing when the per-sample element
 //                                             order is unchanged, else a gather
+//   Reshape of a stored constant           -> a constant, read by MatMul
+//   MatMul by a constant                   -> a bias-free layer of the MLP step
+//   Add of a constant                      -> folded into the bias of the step
+//                                             that produced its operand, else
+//                                             an ADD step (+ activation)
 // Data movement ops are evaluated with the reference's own index formulas
 // (Fortran RESHAPE with ORDER) at a probe batch of 3, which both checks that the
 // op keeps samples independent and yields the per-sample row map.
@@ -149,7 +154,7 @@ bool is_identity(const std::vector<int32_t> &m, int64_t src_rows) {
 struct TVal {
     Shape shape;
     int bdim = 0;
-    int buf = -1;  // -2: value not representable per sample (an error if read)
+    int buf = -1;  // -2: value not representable per sample (an error if read); -3: a stored constant
     int64_t rows() const { return numel(shape) / shape[(size_t)bdim]; }
 };
 
@@ -164,7 +169,8 @@ class Builder {
     std::map<std::string, TVal> vars_;
     std::vector<int> refc_;
     int64_t B0_ = 1;
-    int n_gemm_ = 0, n_lstm_ = 0, n_conv_ = 0, n_max_ = 0, n_avg_ = 0;
+    int n_gemm_ = 0, n_lstm_ = 0, n_conv_ = 0, n_max_ = 0, n_avg_ = 0, n_add_ = 0, n_resh_ = 0;
+    std::map<std::string, HostArray> consts_;  // variables bound to a stored constant (-3)
 
     int new_buf(int64_t rows) {
         plan_->buf_rows.push_back(rows);
@@ -180,6 +186,8 @@ class Builder {
     Status get(const std::string &name, TVal *v) {
         auto it = vars_.find(name);
         if (it == vars_.end()) return Status::Err(ROSENNA_ERR_FORMAT, "architecture reads undefined variable '" + name + "'");
+        if (it->second.buf == -3)
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED, "variable '" + name + "' is a stored constant; only MatMul's second operand may be one");
         if (it->second.buf < 0)
             return Status::Err(ROSENNA_ERR_UNSUPPORTED, "variable '" + name + "' mixes samples after a Reshape; not batched");
         *v = it->second;
@@ -236,7 +244,11 @@ class Builder {
         return S;
     }
 
+    Status push_layer(const std::string &name, const TVal &x, int M, int K, const std::vector<double> &w_mk,
+                      const std::vector<double> &bias);
     Status op_gemm(const PyVal &e);
+    Status op_matmul(const PyVal &e);
+    Status op_add(const PyVal &e);
     Status op_act(const PyVal &e, int act);
     Status op_lstm(const PyVal &e);
     Status op_conv(const PyVal &e);
@@ -247,21 +259,17 @@ class Builder {
     Status finish();
 };
 
-Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90:11-23
-    TVal x;
-    Status st = get(e.at(1).at(0).s, &x);
-    if (!st.ok()) return st;
-    int transB = (int)e.at(1).at(1).as_int();
-    if (n_gemm_ >= (int)mf_.lin.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more Gemm nodes than Gemm weights");
-    const LinearWeights &L = mf_.lin[(size_t)n_gemm_++];
-    if (transB != 1) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gemm with transB=0 (W.inp form) is not supported");
+// Appends Y = X . W^T + bias (W[m][k] = w_mk[m + M*k], the Fortran (M,K)
+// array) as a layer of the MLP step producing x, or starts an MLP step.
+Status Builder::push_layer(const std::string &name, const TVal &x, int M, int K, const std::vector<double> &w_mk,
+                           const std::vector<double> &bias) {
     int rsub = 1;
     if (x.shape.size() == 3 && x.bdim == 1) rsub = (int)x.shape[0];  // (r, batch, K): r sub-rows per sample
     else if (x.shape.size() != 2 || x.bdim != 0)
-        return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gemm input must be (batch, K), got " + shape_str(x.shape));
-    int M = (int)L.w.dims[0], K = (int)L.w.dims[1];
-    if (x.shape.back() != K) return Status::Err(ROSENNA_ERR_SHAPE, "Gemm: input " + shape_str(x.shape) + " vs weights (" + std::to_string(M) + "," + std::to_string(K) + ")");
-    if ((int64_t)L.b.v.size() != M) return Status::Err(ROSENNA_ERR_FORMAT, "Gemm: bias size");
+        return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gemm/MatMul input must be (batch, K), got " + shape_str(x.shape));
+    if (x.shape.back() != K)
+        return Status::Err(ROSENNA_ERR_SHAPE, "Gemm/MatMul: input " + shape_str(x.shape) + " vs weights (" + std::to_string(M) + "," +
+                                                  std::to_string(K) + ")");
     MlpLayer ly;
     ly.K = K;
     ly.M = M;
@@ -269,8 +277,8 @@ Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90
     ly.Mp = (int)round_up(M, 8);
     std::vector<float> wt((size_t)ly.Kp * ly.Mp, 0.f), b((size_t)ly.Mp, 0.f);
     for (int k = 0; k < K; k++)
-        for (int m = 0; m < M; m++) wt[(size_t)k * ly.Mp + m] = (float)L.w.v[(size_t)m + (size_t)M * k];
-    for (int m = 0; m < M; m++) b[(size_t)m] = (float)L.b.v[(size_t)m];
+        for (int m = 0; m < M; m++) wt[(size_t)k * ly.Mp + m] = (float)w_mk[(size_t)m + (size_t)M * k];
+    for (int m = 0; m < M; m++) b[(size_t)m] = (float)bias[(size_t)m];
     ly.w_off = put(wt.data(), wt.size());
     ly.b_off = put(b.data(), b.size());
     if (M <= 256) {  // tensor-core block: rows n < Np hold tf32(W[n][k]), rows Np + n the rounded remainder
@@ -279,12 +287,12 @@ Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90
         std::vector<float> blk((size_t)2 * ly.tc_Np * ly.tc_Kp, 0.f), tb((size_t)ly.tc_Np, 0.f);
         for (int n = 0; n < M; n++)
             for (int k = 0; k < K; k++) {
-                const float w = (float)L.w.v[(size_t)n + (size_t)M * k];
+                const float w = (float)w_mk[(size_t)n + (size_t)M * k];
                 const float hi = tf32_round(w);
                 blk[(size_t)n * ly.tc_Kp + k] = hi;
                 blk[(size_t)(ly.tc_Np + n) * ly.tc_Kp + k] = tf32_round(w - hi);
             }
-        for (int n = 0; n < M; n++) tb[(size_t)n] = (float)L.b.v[(size_t)n];
+        for (int n = 0; n < M; n++) tb[(size_t)n] = (float)bias[(size_t)n];
         ly.tc_w_off = put(blk.data(), blk.size());
         ly.tc_b_off = put(tb.data(), tb.size());
     }
@@ -305,7 +313,132 @@ Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90
     plan_->buf_rows[(size_t)out] = (int64_t)rsub * M;
     Shape os = x.shape;
     os.back() = M;
-    bind(e.at(1).at(0).s, TVal{os, x.bdim, out});
+    bind(name, TVal{os, x.bdim, out});
+    return Status::Ok();
+}
+
+Status Builder::op_gemm(const PyVal &e) {  // modelCreator.fpp:87-89, layers.f90:11-23
+    TVal x;
+    Status st = get(e.at(1).at(0).s, &x);
+    if (!st.ok()) return st;
+    int transB = (int)e.at(1).at(1).as_int();
+    if (n_gemm_ >= (int)mf_.lin.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more Gemm nodes than Gemm weights");
+    const LinearWeights &L = mf_.lin[(size_t)n_gemm_++];
+    if (transB != 1) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gemm with transB=0 (W.inp form) is not supported");
+    int M = (int)L.w.dims[0], K = (int)L.w.dims[1];
+    if ((int64_t)L.b.v.size() != M) return Status::Err(ROSENNA_ERR_FORMAT, "Gemm: bias size");
+    return push_layer(e.at(1).at(0).s, x, M, K, L.w.v, L.b.v);
+}
+
+// matmul2D (layers.f90:25-31): inp1 = MATMUL(inp1, inp2) with inp2 a stored
+// constant (K, M) -- a bias-free layer with W = inp2^T.  Products of two
+// per-sample values, and the rank-3/4 forms, are not batched.
+Status Builder::op_matmul(const PyVal &e) {  // modelCreator.fpp:146-149
+    const std::string &an = e.at(1).at(0).s, &bn = e.at(1).at(1).s;
+    const int rank = (int)e.at(2).at(0).as_int();
+    auto it = consts_.find(bn);
+    auto vb = vars_.find(bn);
+    if (it == consts_.end() || vb == vars_.end() || vb->second.buf != -3)
+        return Status::Err(ROSENNA_ERR_UNSUPPORTED, "MatMul whose second operand is not a stored constant");
+    if (rank != 2) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "MatMul of rank " + std::to_string(rank) + " (only matmul2D is batched)");
+    TVal x;
+    Status st = get(an, &x);
+    if (!st.ok()) return st;
+    const HostArray &W = it->second;
+    if (W.dims.size() != 2) return Status::Err(ROSENNA_ERR_SHAPE, "MatMul: constant operand is not 2-D");
+    const int K = (int)W.dims[0], M = (int)W.dims[1];
+    std::vector<double> w_mk((size_t)M * K), zero((size_t)M, 0.0);
+    for (int m = 0; m < M; m++)
+        for (int k = 0; k < K; k++) w_mk[(size_t)m + (size_t)M * k] = W.v[(size_t)k + (size_t)K * m];
+    return push_layer(an, x, M, K, w_mk, zero);
+}
+
+// Add of a stored constant (modelCreator.fpp:137-144): the adder is broadcast
+// to trueShape by broadc (layers.f90:351-375), RESHAPEd to the operand's shape
+// and added.  Per sample that is one constant per row; it must not depend on
+// the sample.  It folds into the bias of the step that produced the operand
+// when that step is an MLP (no activation yet) or a conv (no ReLU or pooling
+// yet) and the constant is per output unit / channel.
+Status Builder::op_add(const PyVal &e) {
+    const std::string &name = e.at(1).at(0).s;
+    TVal x;
+    Status st = get(name, &x);
+    if (!st.ok()) return st;
+    if (n_add_ >= (int)mf_.add.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more Add nodes than Add layers");
+    const HostArray &A = mf_.add[(size_t)n_add_++];
+    Shape ts = e.at(2).at(0).ints(), sp = e.at(2).at(1).ints();
+    const int rank = (int)e.at(2).at(2).as_int();
+    if (ts.size() != 4 || A.dims.size() != 4 || (sp.size() & 1) || rank < 1 || rank > 4 || rank != (int)x.shape.size())
+        return Status::Err(ROSENNA_ERR_FORMAT, "Add: malformed entry");
+    // broadc: SPREAD along each (dim, copies) pair, RESHAPEd (first elements,
+    // column-major) to trueShape(:dim) + the adder's original trailing dims
+    std::vector<double> cur = A.v;
+    Shape cd = A.dims;
+    for (size_t i = 0; i + 1 < sp.size(); i += 2) {
+        const int d = (int)sp[i];
+        const int64_t n = sp[i + 1];
+        if (d < 1 || d > 4 || n < 1) return Status::Err(ROSENNA_ERR_FORMAT, "Add: spread entry");
+        int64_t P = 1, rest = 1;
+        for (int k = 0; k < d - 1; k++) P *= cd[(size_t)k];
+        for (int k = d - 1; k < 4; k++) rest *= cd[(size_t)k];
+        std::vector<double> spd((size_t)(P * n * rest));
+        for (int64_t b = 0; b < rest; b++)
+            for (int64_t k = 0; k < n; k++)
+                for (int64_t a = 0; a < P; a++) spd[(size_t)(a + P * (k + n * b))] = cur[(size_t)(a + P * b)];
+        Shape nd(4);
+        for (int k = 0; k < 4; k++) nd[(size_t)k] = (i + 2 < sp.size()) ? (k < d ? ts[(size_t)k] : A.dims[(size_t)k]) : ts[(size_t)k];
+        if (numel(nd) > (int64_t)spd.size()) return Status::Err(ROSENNA_ERR_SHAPE, "Add: broadcast shapes do not fit");
+        spd.resize((size_t)numel(nd));
+        cur.swap(spd);
+        cd = nd;
+    }
+    int64_t tn = 1;
+    for (int k = 4 - rank; k < 4; k++) tn *= ts[(size_t)k];
+    if (tn != numel(x.shape) || (int64_t)cur.size() < tn) return Status::Err(ROSENNA_ERR_SHAPE, "Add: adder does not fit its operand");
+    // per-sample rows: element (row r, sample b) of x sits at pre_i + pre*(b + B*post_i)
+    int64_t pre = 1;
+    for (int k = 0; k < x.bdim; k++) pre *= x.shape[(size_t)k];
+    const int64_t B = x.shape[(size_t)x.bdim], rows = x.rows();
+    std::vector<double> c((size_t)rows);
+    for (int64_t r = 0; r < rows; r++) {
+        const int64_t pi = r % pre, qi = r / pre;
+        c[(size_t)r] = cur[(size_t)(pi + pre * (B * qi))];
+        for (int64_t b = 1; b < B; b++)
+            if (cur[(size_t)(pi + pre * (b + B * qi))] != c[(size_t)r])
+                return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Add: the constant differs between the samples of the export batch");
+    }
+    Step *prev = last_producing(x.buf);
+    if (prev && prev->kind == Step::MLP && prev->layers.back().act == ACT_NONE) {
+        MlpLayer &ly = prev->layers.back();
+        const int rs = prev->rsub;  // row t + rs*m
+        bool per_unit = true;
+        for (int64_t r = 0; r < rows && per_unit; r++) per_unit = c[(size_t)r] == c[(size_t)(rs * (r / rs))];
+        if (per_unit) {
+            for (int m = 0; m < ly.M; m++) {
+                plan_->arena[(size_t)(ly.b_off + m)] += (float)c[(size_t)(rs * m)];
+                if (ly.tc_b_off >= 0) plan_->arena[(size_t)(ly.tc_b_off + m)] += (float)c[(size_t)(rs * m)];
+            }
+            return Status::Ok();
+        }
+    }
+    if (prev && prev->kind == Step::CONV && prev->conv && !prev->relu && prev->pool == 0) {
+        bool per_channel = true;  // row oc + OC*(h + Ho*w)
+        for (int64_t r = 0; r < rows && per_channel; r++) per_channel = c[(size_t)r] == c[(size_t)(r % prev->OC)];
+        if (per_channel) {
+            for (int oc = 0; oc < prev->OC; oc++) plan_->arena[(size_t)(prev->b_off + oc)] += (float)c[(size_t)oc];
+            return Status::Ok();
+        }
+    }
+    std::vector<float> cf((size_t)rows);
+    for (int64_t r = 0; r < rows; r++) cf[(size_t)r] = (float)c[(size_t)r];
+    Step s;
+    s.kind = Step::ADD;
+    s.in = x.buf;
+    s.out = new_buf(rows);
+    s.b_off = put(cf.data(), cf.size());
+    plan_->steps.push_back(s);
+    x.buf = s.out;
+    bind(name, x);
     return Status::Ok();
 }
 
@@ -317,6 +450,10 @@ Status Builder::op_act(const PyVal &e, int act) {  // modelCreator.fpp:151-161
     Step *prev = last_producing(x.buf);
     if (prev && prev->kind == Step::MLP && prev->layers.back().act == ACT_NONE) {
         prev->layers.back().act = act;
+        return Status::Ok();
+    }
+    if (prev && prev->kind == Step::ADD && prev->act == ACT_NONE) {
+        prev->act = act;
         return Status::Ok();
     }
     if (prev && prev->kind == Step::CONV && prev->conv && !prev->relu && prev->pool == 0 && act == ACT_RELU) {
@@ -549,7 +686,32 @@ Status Builder::op_reshape(const PyVal &e) {  // modelCreator.fpp:122-130
     const std::string &xn = e.at(1).at(0).s;
     const std::string &on = e.at(2).at(0).s;
     int flag = (int)e.at(e.size() - 1).at(0).as_int();
-    if (flag != 0) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Reshape of a stored constant is not supported");
+    if (flag != 0) {
+        // reshapeLayers(i) = its own axis reversal, then the RESHAPE with the
+        // reversed ORDER: a C-order reshape of the stored constant.  (The
+        // reference keeps the reversed array, so its later calls reshape the
+        // reversed data; this is the first call's result.)
+        if (n_resh_ >= (int)mf_.reshape.size()) return Status::Err(ROSENNA_ERR_FORMAT, "more constant Reshapes than stored constants");
+        const HostArray &A = mf_.reshape[(size_t)n_resh_++];
+        Shape tgt = e.at(3).at(0).ints();
+        if (tgt.empty() || numel(tgt) != A.numel()) return Status::Err(ROSENNA_ERR_SHAPE, "Reshape size mismatch");
+        HostArray out;
+        out.dims = tgt;
+        out.v.resize((size_t)A.numel());
+        const Shape &ad = A.dims;
+        std::vector<int64_t> ia(ad.size(), 0), it(tgt.size(), 0);
+        for (int64_t q = 0; q < A.numel(); q++) {  // q: C-order position in both
+            int64_t la = 0, lt = 0, sa = 1, stt = 1;
+            for (size_t k = 0; k < ad.size(); k++) { la += ia[k] * sa; sa *= ad[k]; }
+            for (size_t k = 0; k < tgt.size(); k++) { lt += it[k] * stt; stt *= tgt[k]; }
+            out.v[(size_t)lt] = A.v[(size_t)la];
+            for (size_t k = ad.size(); k-- > 0;) { if (++ia[k] < ad[k]) break; ia[k] = 0; }
+            for (size_t k = tgt.size(); k-- > 0;) { if (++it[k] < tgt[k]) break; it[k] = 0; }
+        }
+        consts_[on] = std::move(out);
+        bind(on, TVal{tgt, 0, -3});
+        return Status::Ok();
+    }
     TVal x;
     Status st = get(xn, &x);
     if (!st.ok()) return st;
@@ -699,6 +861,8 @@ Status Builder::run() {
         const std::string &op = e.at(0).s;
         Status st;
         if (op == "Gemm") st = op_gemm(e);
+        else if (op == "MatMul") st = op_matmul(e);
+        else if (op == "Add") st = op_add(e);
         else if (op == "Relu") st = op_act(e, ACT_RELU);
         else if (op == "Tanh") st = op_act(e, ACT_TANH);
         else if (op == "Sigmoid") st = op_act(e, ACT_SIGMOID);
@@ -749,6 +913,7 @@ std::string Plan::describe() const {
                 break;
             case Step::GATHER: o << "gather b" << s.in << "->b" << s.out << "\n"; break;
             case Step::ACT: o << "act:" << acts[s.act] << " b" << s.in << "->b" << s.out << "\n"; break;
+            case Step::ADD: o << "add" << (s.act ? "+" : "") << acts[s.act] << " b" << s.in << "->b" << s.out << "\n"; break;
             case Step::COPY: o << "copy b" << s.in << "->b" << s.out << "\n"; break;
         }
     }

@@ -30,7 +30,7 @@ struct MlpLayer {
 };
 
 struct Step {
-    enum Kind { MLP, LSTM, CONV, GATHER, ACT, COPY } kind = MLP;
+    enum Kind { MLP, LSTM, CONV, GATHER, ACT, COPY, ADD } kind = MLP;
     int in = -1, out = -1;  // buffer ids
 
     // MLP (also the head of an LSTM step); rsub sub-rows per sample (row k of
@@ -58,7 +58,8 @@ struct Step {
     // packed weights (MLP: per layer; LSTM/CONV: here)
     int64_t w_off = -1, b_off = -1;
 
-    // GATHER: out row r = in row map[r]; ACT: activation
+    // GATHER: out row r = in row map[r]; ACT: activation; ADD: out row r =
+    // act(in row r + arena[b_off + r])
     int64_t map_off = -1;
     int act = ACT_NONE;
 };

@@ -284,8 +284,10 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 break;
             }
             case Step::ACT:
+            case Step::ADD:
                 e = launch_act(ptr[(size_t)s.in], ld[(size_t)s.in], ptr[(size_t)s.out], ld[(size_t)s.out],
-                               P.buf_rows[(size_t)s.out], cnt, s.act, stream);
+                               P.buf_rows[(size_t)s.out], cnt, s.act, s.kind == Step::ADD ? arena + s.b_off : nullptr,
+                               stream);
                 launches++;
                 break;
         }

@@ -63,6 +63,37 @@ def _reshape_parser(reshape: List[int], true_shape: List[int]) -> List[int]:
     return reshape
 
 
+def _auto_pads(kernel: int, mode: str) -> List[int]:
+    """SAME_UPPER / SAME_LOWER pads from the first kernel dim, as
+    modelParserONNX.py:348-358 and :411-421 compute them."""
+    total = kernel - 1
+    pad = int(total / 2)
+    if total % 2 != 0:
+        return [pad, pad, pad + 1, pad + 1] if mode == "SAME_UPPER" else [pad + 1, pad + 1, pad, pad]
+    return [pad] * 4
+
+
+def _four_d_transform(true_shape: List[int], adder_shape: List[int]) -> List[int]:
+    """fourDTransform, modelParserONNX.py:110-119: each adder dim is placed at
+    the position of its FIRST equal dim in the input shape (counted from the
+    right of a rank-4 shape); dims without an equal are dropped."""
+    new = [1, 1, 1, 1]
+    for dim in adder_shape:
+        if dim in true_shape:
+            new[true_shape.index(dim) - len(true_shape)] = dim
+    return new
+
+
+def _spread_info(true: List[int], fourd: List[int]) -> List[int]:
+    """spreadInfo, modelParserONNX.py:125-131: (1-based dim, copies) pairs where
+    the shapes differ."""
+    ret: List[int] = []
+    for i, d in enumerate(fourd):
+        if true[i] != d:
+            ret += [i + 1, true[i]]
+    return ret
+
+
 def write_model_files(g: Graph, out_dir: str) -> None:
     """Restates the node walk of modelParserONNX.py:151-541 for the supported ops."""
     os.makedirs(out_dir, exist_ok=True)
@@ -183,14 +214,18 @@ def write_model_files(g: Graph, out_dir: str) -> None:
         elif layer == "Reshape":  # :312-331
             f_lines.append(layer)
             src = node.inputs[0]
-            if src in inter or src in input_shapes:
+            # the reference takes the variable form when the source has an
+            # inferred intermediate shape, else the stored-constant form over
+            # an initializer; a graph input without either is taken as a
+            # variable here (the reference stops with a KeyError)
+            if src in inter or (src in input_shapes and src not in init_dims):
                 src_shape = inter.get(src, input_shapes.get(src))
                 new_shape = _reshape_parser([int(v) for v in np.asarray(find_weights(node.inputs[-1])).tolist()], src_shape)
                 arch.append(("Reshape", (io_map[src], len(src_shape)), ["output" + extra], [new_shape], [0]))
                 f_lines.append("0")
             else:
                 new_shape = _reshape_parser([int(v) for v in np.asarray(find_weights(node.inputs[-1])).tolist()], init_dims[src])
-                arch.append(("Reshape", (src, len(init_dims[src])), ["output" + extra], [new_shape], [1]))
+                arch.append(("Reshape", (io_map.get(src, src), len(init_dims[src])), ["output" + extra], [new_shape], [1]))
                 f_lines.append(str(len(init_dims[src])))
                 f_lines.append(" ".join(str(d) for d in init_dims[src]) + " ")
                 w_lines.append(_values_line(find_weights(src)))
@@ -201,6 +236,8 @@ def write_model_files(g: Graph, out_dir: str) -> None:
             f_lines.append(layer)
             attributes = dict(node.attrs)
             pads = list(attributes.get("pads", [0, 0, 0, 0]))
+            if "auto_pad" in attributes:  # :338-358: any auto_pad value, NOTSET included, replaces pads
+                pads = _auto_pads(int(list(attributes["kernel_shape"])[0]), str(attributes["auto_pad"]))
             arch.append(("Conv", [io_map[node.inputs[0]]],
                          [list(attributes.get("dilations", [1, 1])), list(attributes["kernel_shape"]), pads,
                           list(attributes.get("strides", [1, 1]))]))
@@ -219,10 +256,17 @@ def write_model_files(g: Graph, out_dir: str) -> None:
             io_map[node.outputs[0]] = io_map[node.inputs[0]]
         elif layer == "MaxPool":  # :392-425
             f_lines.append(layer)
+            pads = list(node.attrs.get("pads", [0, 0, 0, 0]))
+            auto = str(node.attrs.get("auto_pad", "NOTSET"))
+            if auto != "NOTSET":  # :400-421
+                pads = _auto_pads(int(list(node.attrs["kernel_shape"])[0]), auto)
             arch.append(("MaxPool", [io_map[node.inputs[0]]],
-                         [int(node.attrs.get("ceil_mode", 0)), list(node.attrs.get("pads", [0, 0, 0, 0])),
-                          list(node.attrs["strides"])]))
-            f_lines.append(str(list(node.attrs["kernel_shape"])[0]))
+                         [int(node.attrs.get("ceil_mode", 0)), pads, list(node.attrs["strides"])]))
+            # :423: the window size written is the first int of the node's SECOND
+            # attribute (kernel_shape in torch's sorted order; strides in files
+            # that list kernel_shape, strides, ...)
+            second = list(node.attrs.values())[1]
+            f_lines.append(str(list(second)[0] if isinstance(second, (list, tuple)) else int(second)))
             io_map[node.outputs[0]] = io_map[node.inputs[0]]
         elif layer == "AveragePool":  # :427-439
             f_lines.append(layer)
@@ -230,6 +274,33 @@ def write_model_files(g: Graph, out_dir: str) -> None:
                          [int(node.attrs.get("ceil_mode", 0)), list(node.attrs.get("pads", [0, 0, 0, 0])),
                           list(node.attrs.get("strides", [1, 1]))]))
             f_lines.append(str(list(node.attrs["kernel_shape"])[0]))
+            io_map[node.outputs[0]] = io_map[node.inputs[0]]
+        elif layer == "Add":  # :441-457
+            f_lines.append(layer)
+            src = node.inputs[0]
+            src_shape = list(inter.get(src, input_shapes.get(src, [])))  # (the reference reads value_info only)
+            adder = np.asarray(find_weights(node.inputs[-1]))
+            fourd = _four_d_transform(src_shape, list(adder.shape))
+            true = [1] * (4 - len(src_shape)) + src_shape
+            arch.append(("Add", [io_map[src]], [true, _spread_info(true, fourd), len(src_shape)]))
+            f_lines.append("".join(str(d) + " " for d in fourd))
+            w_lines.append(_values_line(next_weights(node.inputs[1])))
+            io_map[node.outputs[0]] = io_map[src]
+        elif layer == "MatMul":  # :459-488
+            f_lines.append(layer)
+            if node.inputs[0] in io_map and node.inputs[1] in io_map:
+                rank = len(inter.get(node.inputs[0], input_shapes.get(node.inputs[0], [])))
+                arch.append(("MatMul", [io_map[node.inputs[0]], io_map[node.inputs[1]]], [rank]))
+            else:  # a weight operand that is no graph value: written as a bias-free Gemm (transB = 1)
+                f_lines[-1] = "Gemm"
+                arch.append(("Gemm", [io_map[node.inputs[0]], 1], None))
+                numzs = 0
+                for inp in node.inputs[1:]:
+                    numzs = init_dims[inp][0]
+                    f_lines.append(" ".join(str(d) for d in init_dims[inp]) + " ")
+                    w_lines.append(_values_line(next_weights(inp)))
+                f_lines.append(str(numzs))
+                w_lines.append(_values_line(np.zeros(numzs)))
             io_map[node.outputs[0]] = io_map[node.inputs[0]]
         elif layer in ("Relu", "Sigmoid", "Tanh"):  # :495-514
             f_lines.append(layer)

@@ -76,13 +76,15 @@ def test_malformed_and_unsupported_models(tmp_path):
     with pytest.raises(api.RosennaError) as e:
         api.check_model(str(d))
     assert e.value.code == api.ERR_FORMAT
-    # an op the engine does not run
-    shutil.copytree(src, tmp_path / "u")
-    v = (tmp_path / "u" / "variables.fpp").read_text().replace("('Relu', ['input'], [2])", "('Add', ['input'], [2])", 1)
-    (tmp_path / "u" / "variables.fpp").write_text(v)
-    with pytest.raises(api.RosennaError) as e:
-        api.check_model(str(tmp_path / "u"))
-    assert e.value.code == api.ERR_UNSUPPORTED
+    # forms the engine does not batch: an unknown op, a product of two per-sample values
+    for k, entry in enumerate(["('Softmax', ['input'], [2])", "('MatMul', ['input', 'input'], [2])"]):
+        u = tmp_path / f"u{k}"
+        shutil.copytree(src, u)
+        v = (u / "variables.fpp").read_text().replace("('Relu', ['input'], [2])", entry, 1)
+        (u / "variables.fpp").write_text(v)
+        with pytest.raises(api.RosennaError) as e:
+            api.check_model(str(u))
+        assert e.value.code == api.ERR_UNSUPPORTED, entry
     # a broken variables.fpp literal
     shutil.copytree(src, tmp_path / "b")
     (tmp_path / "b" / "variables.fpp").write_text("#:set architecture = [('Gemm', ['input', 1], None\n")

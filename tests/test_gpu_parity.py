@@ -220,3 +220,27 @@ def test_golden_mlps_on_tensor_cores(case, tail, monkeypatch):
     out = api.use_model_rows(xs)[0]
     ref = OracleModel(d).run_batched(n, xs, [1] * len(xs), [1])[0]
     assert_close(out, ref.reshape(out.shape), f"{case} tc n={n}")
+
+
+@pytest.mark.parametrize("ks,pool,pk", [(3, None, 1), (3, "max", 3), (3, "avg", 3), (5, None, 1), (5, "max", 2),
+                                        (5, "avg", 2), (5, "max", 3)])
+def test_conv_kernel_shapes(ks, pool, pk, tmp_path):
+    """Every conv+pool kernel instantiation (3x3 and 5x5 kernels, pool windows
+    1-3) on an odd image (border items), batches with partial warps, against
+    the oracle."""
+    import torch.nn as nn
+    from rosenna_b200 import writer
+
+    torch.manual_seed(ks * 10 + pk)
+    mods = [nn.Conv2d(3, 10, ks, padding=ks // 2), nn.ReLU()]
+    if pool:
+        mods.append((nn.MaxPool2d if pool == "max" else nn.AvgPool2d)(pk, pk))
+    g = writer.export_sequential(mods, [1, 3, 11, 11])
+    writer.write_model_files(g, str(tmp_path))
+    api.initialize(str(tmp_path))
+    assert "conv" in api.plan_description()
+    for n in (1, 45, 1000):
+        ins = [np.random.default_rng(n).uniform(-1, 1, size=(3 * 11 * 11, n)).astype(np.float32)]
+        out = api.use_model_rows(ins)[0]
+        ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
+        assert_close(out, ref.reshape(out.shape), f"k={ks} {pool}{pk} n={n}")
