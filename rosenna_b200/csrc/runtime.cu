@@ -4,12 +4,13 @@
 // the packed weights to every selected GPU.  use_model splits the batch into
 // contiguous sample ranges, one per GPU (one host thread each), and runs the
 // plan on chunks of samples: host->device copies of a chunk's rows, the plan's
-// kernels, device->host copies, with two streams alternating chunks so that the
-// copies of one chunk overlap the kernels of the other.  No collective is
+// kernels, device->host copies, with three streams taking chunks in turn so that
+// the copies of some chunks overlap the kernels of others.  No collective is
 // involved: samples are independent and weights are replicated.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -29,7 +30,7 @@
 namespace rosenna {
 namespace {
 
-constexpr int kSlots = 2;
+constexpr int kSlots = 3;  // chunk streams: one's H2D, another's kernels, a third's D2H
 
 struct Slot {
     cudaStream_t stream = nullptr;
@@ -347,10 +348,17 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
     const Plan &P = g_ctx.plan;
     const int64_t total = b - a;
     if (total <= 0) return Status::Ok();
-    // at least four chunks (of >= 16384 samples) so that one stream's copies
-    // overlap the other stream's kernels; at most 2^20 samples per chunk
+    // Chunks rotate over the slots' streams, so one chunk's copies overlap the
+    // others' kernels.  The first chunk's H2D and the last one's D2H are not
+    // hidden, and every chunk costs a few microseconds of launches: about
+    // sqrt(I/O bytes / 440 KB) chunks (4..64, >= 16384 samples each, at most
+    // 2^20) balances the two (440 KB ~ 8 us of PCIe at 55 GB/s).
     int64_t chunk = std::min<int64_t>(max_chunk(total), (int64_t)1 << 20);
-    chunk = std::min(chunk, std::max<int64_t>(16384, (total + 3) / 4));
+    double io_bytes = 0;
+    for (auto *v : {&P.inputs, &P.outputs})
+        for (auto &io : *v) io_bytes += 4.0 * (double)io.rows * (double)total;
+    const int64_t nch = std::min<int64_t>(64, std::max<int64_t>(4, std::llround(std::sqrt(io_bytes / 440e3))));
+    chunk = std::min(chunk, std::max<int64_t>(16384, (total + nch - 1) / nch));
     chunk = (chunk + 31) / 32 * 32;
     for (int k = 0; k < kSlots; k++) {
         Status st = ensure_scratch(d.slots[k], std::min(chunk, total));
