@@ -8,27 +8,27 @@
 // relative), accumulated in fp32 in tensor memory: fp32-level accuracy from
 // the TF32 tensor pipe.
 //
-// Per CTA (one per SM, persistent over tiles of 128 samples), 8 warps in two
-// groups of four; group g owns output columns [128g, 128g+128) and thread r of a
-// group owns sample row r (TMEM lane r):
-//   - one lane of each group (warps 0 and 5) issues that group's tcgen05.mma
-//     (M=128 samples, N=128 columns, K=8; three per K-step for the 3xTF32
-//     split) into its own TMEM partial buffer, one 32-deep partial per K-chunk
-//     with the small terms first; the group adds each partial into fp32
-//     registers (round-to-nearest: the tensor core truncates while it
-//     accumulates, so long chains inside TMEM lose accuracy).  A group issues
-//     the next chunk's MMAs as soon as it has drained the previous partial; the
-//     halves take turns in the tensor pipe, so one drains while the other
-//     computes.  Issuing holds the issuing warp until its MMAs are nearly done,
-//     so the issuers' warps stage nothing.
+// Per CTA (one per SM, persistent over tiles of 128 samples): two groups of
+// four warps; group g owns output columns [128g, 128g+128) and thread r of a
+// group owns sample row r (TMEM lane r); a third warpgroup produces:
+//   - one lane issues every tcgen05.mma (M=128 samples, N=128 columns, K=8;
+//     three per K-step for the 3xTF32 split), chunk by chunk, group 0's half
+//     then group 1's, each into that group's TMEM partial buffer: one 32-deep
+//     partial per K-chunk with the small terms first.  A group adds each
+//     partial into fp32 registers (round-to-nearest: the tensor core truncates
+//     while it accumulates, so long chains inside TMEM lose accuracy) while the
+//     other group's MMAs run.  Issuing holds the issuing thread until its MMAs
+//     are nearly done (the MMA queue is shallow), which is why it has no other
+//     work.
 //   - one lane streams [Wh | Wl] K-chunks of 32 (128-byte swizzled rows) by TMA
 //     into a 2-stage ring, two chunks ahead of the MMAs.
 //   - the A operand of layer 0 is the input tile, of later layers the previous
 //     layer's activations (kept in TMEM), split into tf32 hi/lo in a 2-stage
-//     smem ring by the six staging warps (16-wide K halves of each chunk).
+//     smem ring by the group warps (each a 16-wide K half of its rows).
 //   - after the last K-chunk a group adds bias, applies the activation and
-//     writes its half to TMEM for the next layer (handed over to the other
-//     group through an mbarrier), or to global memory.
+//     writes its half to TMEM for the next layer (handed over through an
+//     mbarrier; group 0 stages the next layer's first two chunks straight from
+//     its registers), or to global memory.
 // Every wait on an mbarrier is bounded; on time-out the kernel records an error
 // code and where it waited in `err`, lets every role finish, frees TMEM and
 // returns.
@@ -45,8 +45,8 @@ namespace {
 constexpr int kBM = 128;                 // samples per tile (UMMA M)
 constexpr int kKC = 32;                  // K per chunk: 32 fp32 = one 128-byte swizzle row
 constexpr int kNMax = 256;               // widest layer (UMMA N)
-constexpr int kThreadsTc = 256;           // two groups of four warps (2 warps per SMSP: up to 255 registers)
-constexpr int kStagers = 6 * 32;          // threads that stage A (all but the issuers' warps)
+constexpr int kThreadsTc = 256;           // lstm_tc_kernel: two groups of four warps (up to 255 registers)
+constexpr int kStagers = 6 * 32;          // lstm_tc_kernel: threads that stage A (all but the issuers' warps)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTCol = 0;             // TMEM cols [0,256): previous layer's activations
 constexpr uint32_t kPCol = 256;           // TMEM cols [256,512): partial sums of column half h at 256+128h
@@ -75,9 +75,6 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
@@ -317,77 +314,60 @@ __device__ __forceinline__ void load_b(const TcArgs &p, uint8_t *b0, uint64_t *b
     tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
 }
 
-// Issues the MMAs of this group's half for chunk jj (layer l, K-chunk c) as
-// partial number pi: waits for the B and A stages and for the group to have
-// drained the previous partial, then one 32-deep product with the small terms
-// (Al*Wh, Ah*Wl) first and Ah*Wh last, so the truncating accumulation adds the
-// big terms to an accumulator that holds only small ones.  Commits p_full (the
-// partial) and a_empty (this group's use of the A/B stage).
-__device__ __forceinline__ bool issue_chunk(const TcArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
-                                            uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full,
-                                            uint64_t *p_empty, uint32_t tmem, int g, int l, int c, uint32_t jj,
-                                            uint32_t pi) {
-    const int s = jj & 1;
-    const int where = (l << 8) | c;
-    if (!mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, where, (int)jj, g, 0)) return false;
-    if (!mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, where, (int)jj, g, 0)) return false;
-    if (!mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, where, (int)pi, (int)jj, 0)) return false;
-    tc_fence_after();
-    const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
-    const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
-    const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;  // rows 128g.. of the B tiles
-    const uint64_t bh = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile)) + boff;
-    const uint64_t bl = desc_kmajor_sw128(smem_u32(b0 + s * 2 * kBTile + kBTile)) + boff;
-    const uint32_t idesc = idesc_tf32(min(128, p.L[l].Np - 128 * g));
+// tcgen05.mma kind::tf32 with the descriptors given by their low words (start
+// address and LBO) over the common high word of desc_kmajor_sw128 (SBO 1024 B,
+// version 1, 128-byte swizzle): one register per descriptor.
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+__device__ __forceinline__ void umma_tf32_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                             uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "mov.b64 da, {%1, %5};\n\t"
+        "mov.b64 db, {%2, %5};\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(acc), "n"(kDescHi));
+}
+
+// The MMAs of group g's column half for the A/B ring stage s (layer l): one
+// 32-deep product into the group's partial buffer with the small terms (Al*Wh,
+// Ah*Wl) first and Ah*Wh last, so the truncating accumulation adds the big
+// terms to an accumulator that holds only small ones.
+__device__ __forceinline__ void issue_half(uint32_t a_s, uint32_t b_s, uint32_t tmem, int g, int np, int s) {
+    // a_s / b_s: shared addresses of the rings; the address fields stay below 2^14
+    // (shared memory < 256 KB), so advancing the low word never carries
+    const uint32_t ah = desc_lo(a_s + (uint32_t)s * 2 * kATile);
+    const uint32_t al = desc_lo(a_s + (uint32_t)s * 2 * kATile + kATile);
+    const uint32_t boff = (uint32_t)(g * 128 * 128) >> 4;  // rows 128g.. of the B tiles
+    const uint32_t bh = desc_lo(b_s + (uint32_t)s * 2 * kBTile) + boff;
+    const uint32_t bl = desc_lo(b_s + (uint32_t)s * 2 * kBTile + kBTile) + boff;
+    const uint32_t idesc = idesc_tf32(min(128, np - 128 * g));
     const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
 #pragma unroll
     for (int kk = 0; kk < kKC / 8; kk++) {
-        const uint64_t adv = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
-        umma_tf32(d, al + adv, bh + adv, idesc, kk);
-        umma_tf32(d, ah + adv, bl + adv, idesc, 1);
+        const uint32_t adv = (uint32_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along K
+        umma_tf32_lo(d, al + adv, bh + adv, idesc, kk);
+        umma_tf32_lo(d, ah + adv, bl + adv, idesc, 1);
     }
 #pragma unroll
     for (int kk = 0; kk < kKC / 8; kk++) {
-        const uint64_t adv = (uint64_t)((kk * 32) >> 4);
-        umma_tf32(d, ah + adv, bh + adv, idesc, 1);
+        const uint32_t adv = (uint32_t)((kk * 32) >> 4);
+        umma_tf32_lo(d, ah + adv, bh + adv, idesc, 1);
     }
-    umma_commit(&p_full[g]);
-    umma_commit(&a_empty[s]);  // the stage is released when these MMAs complete
-    return true;
-}
-
-// issue_chunk in the halves' turn order: group 1 takes chunk jj only after
-// group 0 has issued it, so the two halves' MMAs alternate in the tensor pipe
-// and one half drains while the other computes.  Group 0 issues every chunk and
-// arrives on turn[jj&1]; group 1 waits there for every chunk (also one it has
-// no columns of).  Two barriers by chunk parity: group 0 cannot issue chunk
-// jj+2 before group 1 issued jj (the A stage of jj+2 is staged only after
-// chunk jj is consumed), so neither barrier gets a phase ahead of its waiter.
-__device__ __forceinline__ bool wait_turn(const TcArgs &p, uint64_t *turn, int l, int c, uint32_t jj) {
-    return mbar_wait(&turn[jj & 1], (jj >> 1) & 1, p.err, 8, (l << 8) | c, (int)jj, 0, 0);
-}
-__device__ __forceinline__ bool issue_in_turn(const TcArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
-                                              uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full,
-                                              uint64_t *p_empty, uint64_t *turn, uint32_t tmem, int g, int l, int c,
-                                              uint32_t jj, uint32_t &pi) {
-    if (g == 1 && !wait_turn(p, turn, l, c, jj)) return false;
-    if (!issue_chunk(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, tmem, g, l, c, jj, pi)) return false;
-    pi++;
-    if (g == 0) mbar_arrive(&turn[jj & 1]);
-    return true;
 }
 
 // Layer hand-over by group 0 (which owns columns 0..127): applies the
 // activation in place, stages A chunk C0/32 of the next layer (columns
-// C0..C0+31) straight from the registers into ring slot j&1, and arrives on its
-// a_full for the six staging warps (warps 0 and 1 count twice: 64*2 + 64 = 192).
+// C0..C0+31) straight from the registers into ring slot j&1, and arrives on
+// its a_full (with group 1's empty arrivals: every chunk's a_full counts 256).
 template <int ACT>
 __device__ __forceinline__ void act_in_place(float (&acc)[128]) {
 #pragma unroll
     for (int i = 0; i < 128; i++) acc[i] = tc_act<ACT>(acc[i]);
 }
 template <int C0>
-__device__ __forceinline__ void stage_from_regs(uint8_t *a0, uint64_t *a_full, int r, int warp, const float (&acc)[128],
+__device__ __forceinline__ void stage_from_regs(uint8_t *a0, uint64_t *a_full, int r, const float (&acc)[128],
                                                 uint32_t j) {
     uint8_t *ahi = a0 + (j & 1) * 2 * kATile;
 #pragma unroll
@@ -399,7 +379,7 @@ __device__ __forceinline__ void stage_from_regs(uint8_t *a0, uint64_t *a_full, i
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
-    mbar_arrive_n(&a_full[j & 1], warp < 2 ? 2u : 1u);
+    mbar_arrive(&a_full[j & 1]);
 }
 
 // Applies the activation (the accumulators started at the bias) and writes
@@ -510,7 +490,18 @@ __device__ __forceinline__ bool run_tail(const TcArgs &p, uint8_t *base, float (
     return true;
 }
 
-__global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
+// Warp roles (12 warps, three warpgroups): warps 0-3 and 4-7 are the two
+// column groups (drain, stage A, layer ends, tail), at 232 registers; warp 8
+// lane 0 issues every MMA of both groups and warp 9 lane 0 streams B, at 40
+// registers (setmaxnreg moves registers from the producer warpgroup to the
+// groups: 128*40 + 256*232 = 384*168, the launch's registers).  No drain or
+// staging waits behind an issuing thread held by the shallow MMA queue.
+constexpr int kThreadsWs = 384;
+constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to 8; setmaxnreg's pool
+constexpr int kConsumerRegs = 232, kProducerRegs = 40;
+static_assert(kThreadsWs * kLaunchRegs >= 256 * kConsumerRegs + 128 * kProducerRegs, "register split");
+
+__global__ void __launch_bounds__(kThreadsWs, 1) mlp_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *const b0 = base;           // B stage s: hi at b0 + s*2*kBTile, lo + kBTile
@@ -519,47 +510,36 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
     uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
-    uint64_t *const turn = bars + 16;  // [2], by chunk parity
+    uint64_t *const mma_done = bars + 11;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = warp >> 2, quad = warp & 3;
-    const int r = quad * 32 + lane;                    // sample row in the tile == TMEM lane
-    // Issuing MMAs holds a thread until they are nearly done (the tensor pipe
-    // queues few), so the issuers' warps (0 and 5) stage nothing: warps 4 and 1
-    // stage both K halves of TMEM lane quadrants 0 and 1, the other warps their
-    // group's half.
-    const bool issuer = lane == 0 && (warp == 0 || warp == 5);  // issues this group's MMAs
-    const int halves = (warp == 0 || warp == 5) ? 0 : (warp == 1 || warp == 4) ? 3 : 1 << g;
-    const bool loader = warp == 2 && lane == 0;                 // issues the TMA loads
-    const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;  // records this group's position on error
     const int nl = p.nlayers;
     const int ntiles = (int)((p.n + kBM - 1) / kBM);
 
-    for (int i = tid; i < nl * kNMax; i += kThreadsTc) {
+    for (int i = tid; i < nl * kNMax; i += kThreadsWs) {
         const int l = i / kNMax, j = i - l * kNMax;
         sbias[i] = j < p.L[l].Np ? p.arena[p.L[l].b_off + j] : 0.f;
     }
     if (p.tail_n > 0) {  // zero beyond K and tail_np: those activations meet zero weights
         float *stail = reinterpret_cast<float *>(base + kSmemB + kSmemA + kSmemBias);
-        for (int i = tid; i < kNMax * kTcTailMaxN; i += kThreadsTc) {
+        for (int i = tid; i < kNMax * kTcTailMaxN; i += kThreadsWs) {
             const int k = i / kTcTailMaxN, n = i - k * kTcTailMaxN;
             stail[i] = (k < p.tail_kp && n < p.tail_np) ? p.arena[p.tail_w_off + (long long)k * p.tail_np + n] : 0.f;
         }
-        for (int i = tid; i < kTcTailMaxN; i += kThreadsTc)
+        for (int i = tid; i < kTcTailMaxN; i += kThreadsWs)
             sbias[nl * kNMax + i] = i < p.tail_np ? p.arena[p.tail_b_off + i] : 0.f;
     }
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
-            mbar_init(&a_full[s], kStagers);
-            mbar_init(&a_empty[s], 2);          // one tcgen05.commit per group
+            mbar_init(&a_full[s], 256);   // every group thread stages a K half of each chunk
+            mbar_init(&a_empty[s], 1);    // one tcgen05.commit after both groups' MMAs
             mbar_init(&p_full[s], 1);
-            mbar_init(&p_empty[s], kBM);
+            mbar_init(&p_empty[s], kBM);  // the group's 128 threads have drained the partial
         }
-        mbar_init(t_ready, kThreadsTc);
-        mbar_init(&turn[0], 1);
-        mbar_init(&turn[1], 1);
+        mbar_init(t_ready, 256);
+        mbar_init(mma_done, 1);
         mbar_init(bars + 12, kBM);  // tail exchange: full, empty
         mbar_init(bars + 13, kBM);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -573,205 +553,219 @@ __global__ void __launch_bounds__(kThreadsTc, 1) mlp_tc_kernel(const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
 
-    uint32_t b_issued = 0, b_done = 0;  // loader: chunks loaded / seen consumed
-    if (loader) {
-        for (int l = 0; l < nl; l++) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.maps[l]) : "memory");
-        int t = blockIdx.x, l = 0, c = 0;
-        if (t < ntiles) {
-            load_b(p, b0, b_full, l, c, b_issued++);
-            if (chunk_after(p, ntiles, t, l, c, 1)) load_b(p, b0, b_full, l, c, b_issued++);
-        }
-    }
-
-    // j: chunks seen consumed; pu / pi: partials of this group drained / issued;
-    // tb: T hand-overs between layers seen
-    // xt: tail exchanges seen
-    uint32_t j = 0, pu = 0, pi = 0, tb = 0, xt = 0;
-    bool ok = true;
-    float acc[128];
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        for (int l = 0; l < nl && ok; l++) {
-            const int nch = p.L[l].nch, Np = p.L[l].Np;
-            const bool has_half = 128 * g < Np;
-            if (l == 0) {  // the input layer: chunks 0 and 1 from global memory
-                if (halves) {
-                    stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 0, j);
-                    if (nch > 1) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, 1, j + 1);
-                }
-                if (has_half && issuer)
-                    ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi);
-            } else if (g == 1 && has_half && issuer) {
-                // group 0 staged chunks 0 and 1 from its registers and issued chunk 0 at
-                // the previous layer's end; group 1's half of chunk 0 follows it
-                ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l, 0, j, pi);
-            }
-            ok = __all_sync(0xffffffffu, ok);
-            {  // while chunk 0 computes: the accumulators start at the bias (zero beyond Np)
-                const uint32_t b_addr = smem_u32(sbias + l * kNMax + 128 * g);
-#pragma unroll
-                for (int q = 0; q < 32; q++)
-                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                                 : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
-                                 : "r"(b_addr + 16u * q));
-            }
-            for (int c = 0; c < nch && ok; c++) {
-                const uint32_t jj = j + (uint32_t)c;
-                const int s = jj & 1;
-                if (has_half) {
-                    // partial of chunk c: add it into acc, four TMEM loads in flight
-                    ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 8) | c, (int)pu,
-                                                           (int)jj, slot));
-                    if (!ok) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int q0 = 0; q0 < 8; q0 += 4) {
-                        if (128 * g + 16 * q0 < Np) {
-                            uint32_t v[4][16];
-#pragma unroll
-                            for (int u = 0; u < 4; u++)
-                                if (128 * g + 16 * (q0 + u) < Np)
-                                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int u = 0; u < 4; u++)
-                                if (128 * g + 16 * (q0 + u) < Np) {
-#pragma unroll
-                                    for (int e = 0; e < 16; e += 2)
-                                        add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e], v[u][e + 1]);
-                                }
+    if (warp >= 8) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+        if (warp == 8 && lane == 0) {
+            // ---- MMA issuer: chunk by chunk, group 0's half then group 1's ----
+            uint32_t jj = 0, pi0 = 0, pi1 = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
+                for (int l = 0; l < nl && ok; l++) {
+                    const int nch = p.L[l].nch, Np = p.L[l].Np;
+                    for (int c = 0; c < nch && ok; c++, jj++) {
+                        const int s = jj & 1, where = (l << 8) | c;
+                        ok = mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, where, (int)jj, 0, 2) &&
+                             mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, where, (int)jj, 0, 2);
+                        for (int g = 0; g < 2 && ok; g++) {
+                            if (128 * g >= Np) continue;
+                            uint32_t &pi = g ? pi1 : pi0;
+                            ok = mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, where, (int)pi, (int)jj, 2);
+                            if (!ok) break;
+                            tc_fence_after();
+                            issue_half(smem_u32(a0), smem_u32(b0), tmem, g, Np, s);
+                            umma_commit(&p_full[g]);
+                            pi++;
                         }
+                        if (ok) umma_commit(&a_empty[s]);  // the stage is free when these MMAs complete
                     }
-                    tc_fence_before();
-                    mbar_arrive(&p_empty[g]);
-                    pu++;
-                    // the next chunk's MMAs go in before this thread stages anything
-                    if (issuer && c + 1 < nch)
-                        ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, l,
-                                           c + 1, jj + 1, pi);
-                    ok = __all_sync(0xffffffffu, ok);
-                    if (!ok) break;
-                } else if (issuer) {
-                    // a group without columns in this layer releases the stage at once (group
-                    // 1 after its turn, which keeps the turn phases in step)
-                    ok = g == 0 || wait_turn(p, turn, l, c, jj);
-                    umma_commit(&a_empty[s]);
                 }
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                if (c == 0 && l > 0) {  // T of the previous layer: both halves written (before chunk 2 is staged)
-                    ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, l, (int)tb, (int)j, slot));
-                    tb++;
-                    tc_fence_after();
-                    if (!ok) break;
-                }
-                // group 0 takes the last chunk's a_empty at the hand-over to the next layer
-                if (g == 0 && c == nch - 1 && l + 1 < nl) break;
-                // Every thread observes the consumption of every chunk in order, so every
-                // later wait on any ring barrier is at most one phase ahead: no aliasing.
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)pu, slot));
-                if (!ok) break;
-                if (loader) {  // ring stage s is free: load the chunk two ahead
-                    b_done = jj + 1;
+            // every MMA issued here has completed before TMEM and shared memory go away
+            umma_commit(mma_done);
+            mbar_wait(mma_done, 0, p.err, 0);
+        } else if (warp == 9 && lane == 0) {
+            // ---- B loader: two chunks ahead of the MMAs ----
+            for (int l = 0; l < nl; l++) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.maps[l]) : "memory");
+            uint32_t issued = 0, jj = 0;
+            int t = blockIdx.x, l = 0, c = 0;
+            if (t < ntiles) {
+                load_b(p, b0, b_full, 0, 0, issued++);
+                int t1 = t, l1 = 0, c1 = 0;
+                if (chunk_after(p, ntiles, t1, l1, c1, 1)) load_b(p, b0, b_full, l1, c1, issued++);
+                bool more = true;
+                while (more) {
+                    if (!mbar_wait(&a_empty[jj & 1], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)issued, 1))
+                        break;
                     int t2 = t, l2 = l, c2 = c;
-                    if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, b_issued++);
+                    if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, issued++);
+                    jj++;
+                    more = chunk_after(p, ntiles, t, l, c, 1);
                 }
-                if (c + 2 < nch && halves) stage_halves(p, a0, a_full, lane_base, r, halves, t, l, c + 2, jj + 2);
             }
-            j += (uint32_t)nch;
-            if (!ok) break;
-            const bool last = l + 1 == nl;
-            const bool to_out = last && p.tail_n == 0;  // else T, for the next layer or the tail
-            if (last && !to_out) {  // the CUDA-core tail takes this layer's activations from acc
-                const float *stail = reinterpret_cast<const float *>(base + kSmemB + kSmemA + kSmemBias);
-                const int np_prev = has_half ? Np : 0;
-                if (p.tail_np == 8) {
-                    float o[8];
-                    switch (p.L[l].act) {
-                        case 1: tail_dots<1, 8>(o, acc, stail, g, np_prev); break;
-                        case 2: tail_dots<2, 8>(o, acc, stail, g, np_prev); break;
-                        case 3: tail_dots<3, 8>(o, acc, stail, g, np_prev); break;
-                        default: tail_dots<0, 8>(o, acc, stail, g, np_prev); break;
-                    }
-                    ok = run_tail<8>(p, base, o, g, r, t, xt, slot);
-                } else {
-                    float o[16];
-                    switch (p.L[l].act) {
-                        case 1: tail_dots<1, 16>(o, acc, stail, g, np_prev); break;
-                        case 2: tail_dots<2, 16>(o, acc, stail, g, np_prev); break;
-                        case 3: tail_dots<3, 16>(o, acc, stail, g, np_prev); break;
-                        default: tail_dots<0, 16>(o, acc, stail, g, np_prev); break;
-                    }
-                    ok = run_tail<16>(p, base, o, g, r, t, xt, slot);
+            // copies issued but not seen consumed (an error path) land first: the
+            // last load of each slot completes after the earlier ones
+            for (uint32_t k = issued > 2 ? issued - 2 : 0; k < issued; k++)
+                mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
+        }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
+        const int g = warp >> 2, quad = warp & 3;
+        const int r = quad * 32 + lane;  // sample row in the tile == TMEM lane
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;  // records this group's position on error
+        // j: chunks seen consumed; pu: partials of this group drained; tb: T
+        // hand-overs between layers seen; xt: tail exchanges seen
+        uint32_t j = 0, pu = 0, tb = 0, xt = 0;
+        bool ok = true;
+        float acc[128];
+        if (g == 1) {  // group 1's arrival for chunk 1 when it is a hand-over chunk (no chunk two before)
+            int t1 = blockIdx.x, l1 = 0, c1 = 0;
+            if (t1 < ntiles && chunk_after(p, ntiles, t1, l1, c1, 1) && l1 > 0 && c1 < 2) mbar_arrive(&a_full[1]);
+        }
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int l = 0; l < nl && ok; l++) {
+                const int nch = p.L[l].nch, Np = p.L[l].Np;
+                const bool has_half = 128 * g < Np;
+                if (l == 0) {  // the input layer: chunks 0 and 1 from global memory
+                    stage_halves(p, a0, a_full, lane_base, r, 1 << g, t, l, 0, j);
+                    if (nch > 1) stage_halves(p, a0, a_full, lane_base, r, 1 << g, t, l, 1, j + 1);
                 }
-            } else if (!last && g == 0) {
-                // Hand-over by group 0: chunks 0 and 1 of the next layer straight from
-                // the registers, chunk 0 issued at once (behind group 1's last MMAs),
-                // columns 64..127 into T for the staging warps.
-                switch (p.L[l].act) {
-                    case 1: act_in_place<1>(acc); break;
-                    case 2: act_in_place<2>(acc); break;
-                    case 3: act_in_place<3>(acc); break;
-                    default: break;
-                }
-                const int nl1 = l + 1;
-                stage_from_regs<0>(a0, a_full, r, warp, acc, j);
-                if (issuer)
-                    ok = issue_in_turn(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, 0, nl1, 0, j,
-                                       pi);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
+                {  // the accumulators start at the bias (zero beyond Np)
+                    const uint32_t b_addr = smem_u32(sbias + l * kNMax + 128 * g);
 #pragma unroll
-                for (int q = 4; q < 8; q++) {
-                    float v[16];
+                    for (int q = 0; q < 32; q++)
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
+                                     : "r"(b_addr + 16u * q));
+                }
+                for (int c = 0; c < nch && ok; c++) {
+                    const uint32_t jj = j + (uint32_t)c;
+                    const int s = jj & 1;
+                    if (has_half) {
+                        // partial of chunk c: add it into acc, four TMEM loads in flight
+                        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 8) | c, (int)pu,
+                                                               (int)jj, slot));
+                        if (!ok) break;
+                        tc_fence_after();
 #pragma unroll
-                    for (int e = 0; e < 16; e++) v[e] = acc[16 * q + e];
-                    tmem_st16(lane_base + kTCol + (uint32_t)(16 * q), v);
-                }
-                // the last chunk of this layer (its slot takes chunk 1 of the next)
-                const uint32_t jl = j - 1;
-                ok = __all_sync(0xffffffffu, mbar_wait(&a_empty[jl & 1], (jl >> 1) & 1, p.err, 5,
-                                                       (l << 8) | (nch - 1), (int)jl, (int)pu, slot));
-                if (!ok) break;
-                if (loader) {
-                    b_done = jl + 1;
-                    int t2 = t, l2 = l, c2 = nch - 1;
-                    if (chunk_after(p, ntiles, t2, l2, c2, 2)) load_b(p, b0, b_full, l2, c2, b_issued++);
-                }
-                if (p.L[nl1].nch > 1) stage_from_regs<32>(a0, a_full, r, warp, acc, j + 1);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                mbar_arrive(t_ready);
-            } else if (has_half || !last) {
-                if (has_half) {
-                    switch (p.L[l].act) {
-                        case 1: finalize_half<1>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
-                        case 2: finalize_half<2>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
-                        case 3: finalize_half<3>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
-                        default: finalize_half<0>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                        for (int q0 = 0; q0 < 8; q0 += 4) {
+                            if (128 * g + 16 * q0 < Np) {
+                                uint32_t v[4][16];
+#pragma unroll
+                                for (int u = 0; u < 4; u++)
+                                    if (128 * g + 16 * (q0 + u) < Np)
+                                        tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int u = 0; u < 4; u++)
+                                    if (128 * g + 16 * (q0 + u) < Np) {
+#pragma unroll
+                                        for (int e = 0; e < 16; e += 2)
+                                            add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e],
+                                                 v[u][e + 1]);
+                                    }
+                            }
+                        }
+                        tc_fence_before();
+                        mbar_arrive(&p_empty[g]);
+                        pu++;
+                    }
+                    if (c == 0 && l > 0) {  // T of the previous layer: both halves written (before chunk 2 is staged)
+                        ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, l, (int)tb, (int)j, slot));
+                        tb++;
+                        tc_fence_after();
+                        if (!ok) break;
+                    }
+                    // group 0 takes the last chunk's a_empty at the hand-over to the next layer
+                    if (g == 0 && c == nch - 1 && l + 1 < nl) break;
+                    // Every thread observes the consumption of every chunk in order, so every
+                    // later wait on any ring barrier is at most one phase ahead: no aliasing.
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)pu, slot));
+                    if (!ok) break;
+                    if (c + 2 < nch) {
+                        stage_halves(p, a0, a_full, lane_base, r, 1 << g, t, l, c + 2, jj + 2);
+                    } else if (g == 1) {
+                        // Chunks 0 and 1 of a later layer are staged by group 0 alone at its
+                        // hand-over; group 1 arrives for them here, after seeing the chunk two
+                        // before consumed, so no chunk can be consumed twice over before group
+                        // 1 has seen the one two before it (parity waits stay unambiguous).
+                        int t2 = t, l2 = l, c2 = c;
+                        if (chunk_after(p, ntiles, t2, l2, c2, 2) && l2 > 0 && c2 < 2) mbar_arrive(&a_full[s]);
                     }
                 }
-                if (!last) {  // group 1: its half of T for the next layer
+                j += (uint32_t)nch;
+                if (!ok) break;
+                const bool last = l + 1 == nl;
+                const bool to_out = last && p.tail_n == 0;  // else T, for the next layer or the tail
+                if (last && !to_out) {  // the CUDA-core tail takes this layer's activations from acc
+                    const float *stail = reinterpret_cast<const float *>(base + kSmemB + kSmemA + kSmemBias);
+                    const int np_prev = has_half ? Np : 0;
+                    if (p.tail_np == 8) {
+                        float o[8];
+                        switch (p.L[l].act) {
+                            case 1: tail_dots<1, 8>(o, acc, stail, g, np_prev); break;
+                            case 2: tail_dots<2, 8>(o, acc, stail, g, np_prev); break;
+                            case 3: tail_dots<3, 8>(o, acc, stail, g, np_prev); break;
+                            default: tail_dots<0, 8>(o, acc, stail, g, np_prev); break;
+                        }
+                        ok = run_tail<8>(p, base, o, g, r, t, xt, slot);
+                    } else {
+                        float o[16];
+                        switch (p.L[l].act) {
+                            case 1: tail_dots<1, 16>(o, acc, stail, g, np_prev); break;
+                            case 2: tail_dots<2, 16>(o, acc, stail, g, np_prev); break;
+                            case 3: tail_dots<3, 16>(o, acc, stail, g, np_prev); break;
+                            default: tail_dots<0, 16>(o, acc, stail, g, np_prev); break;
+                        }
+                        ok = run_tail<16>(p, base, o, g, r, t, xt, slot);
+                    }
+                } else if (!last && g == 0) {
+                    // Hand-over by group 0: chunk 0 of the next layer straight from the
+                    // registers into the slot of chunk j-2 (seen consumed), so the issuer can
+                    // queue it behind group 1's last MMAs; columns 64..127 into T for the
+                    // other chunks; chunk 1 into the last chunk's slot once it is consumed.
+                    switch (p.L[l].act) {
+                        case 1: act_in_place<1>(acc); break;
+                        case 2: act_in_place<2>(acc); break;
+                        case 3: act_in_place<3>(acc); break;
+                        default: break;
+                    }
+                    const int nl1 = l + 1;
+                    stage_from_regs<0>(a0, a_full, r, acc, j);
+#pragma unroll
+                    for (int q = 4; q < 8; q++) {
+                        float v[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) v[e] = acc[16 * q + e];
+                        tmem_st16(lane_base + kTCol + (uint32_t)(16 * q), v);
+                    }
+                    const uint32_t jl = j - 1;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&a_empty[jl & 1], (jl >> 1) & 1, p.err, 5,
+                                                           (l << 8) | (nch - 1), (int)jl, (int)pu, slot));
+                    if (!ok) break;
+                    if (p.L[nl1].nch > 1) stage_from_regs<32>(a0, a_full, r, acc, j + 1);
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     tc_fence_before();
                     mbar_arrive(t_ready);
+                } else if (has_half || !last) {
+                    if (has_half) {
+                        switch (p.L[l].act) {
+                            case 1: finalize_half<1>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                            case 2: finalize_half<2>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                            case 3: finalize_half<3>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                            default: finalize_half<0>(p, acc, p.L[l].N, g, lane_base, to_out, t, r); break;
+                        }
+                    }
+                    if (!last) {  // group 1: its half of T for the next layer
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        tc_fence_before();
+                        mbar_arrive(t_ready);
+                    }
                 }
             }
         }
     }
-    // Before TMEM and shared memory go away: the issuers' MMAs have completed
-    // (each group saw its last partial, every chunk's a_empty) and the loader's
-    // copies have landed.  On an error path, wait (bounded) for what is in flight:
-    // an extra commit on p_full completes when all of this thread's MMAs are done,
-    // its phases are waited in order.
-    if (issuer) {
-        umma_commit(&p_full[g]);
-        for (uint32_t k = pu; k <= pi; k++) mbar_wait(&p_full[g], k & 1, p.err, 0);
-    }
-    if (loader)  // chunks loaded but not seen consumed (only on an error path) must land first
-        for (uint32_t k = b_done; k < b_issued; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -1151,7 +1145,14 @@ cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st) {
     const long long tiles = (a.n + kBM - 1) / kBM;
     const int grid = (int)(tiles < num_sms ? tiles : num_sms);
     if (grid <= 0) return cudaSuccess;
-    mlp_tc_kernel<<<grid, kThreadsTc, mlp_tc_smem_bytes(), st>>>(a);
+    // setmaxnreg redistributes the registers the block was launched with: the
+    // split only fits (and only ever completes) at exactly kLaunchRegs a thread
+    static const int regs = [] {
+        cudaFuncAttributes fa{};
+        return cudaFuncGetAttributes(&fa, mlp_tc_kernel) == cudaSuccess ? fa.numRegs : -1;
+    }();
+    if (regs != kLaunchRegs) return cudaErrorInvalidConfiguration;
+    mlp_tc_kernel<<<grid, kThreadsWs, mlp_tc_smem_bytes(), st>>>(a);
     return cudaGetLastError();
 }
 
