@@ -204,11 +204,13 @@ __device__ __forceinline__ uint32_t idesc_tf32(int N) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t tf32_rna(float x) {
-    uint32_t y;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(y) : "f"(x));
-    return y;
-}
+// Round to tf32 (10 explicit mantissa bits), to nearest with ties away from
+// zero: add half a tf32 ulp to the magnitude bits and clear the 13 low bits.
+// Two integer-pipe operations per value; the conversion instruction runs at a
+// fraction of that rate, and staging converts 64 values per thread per chunk.
+// A carry out of the mantissa rounds up into the exponent, as it should (to
+// infinity past the largest float).
+__device__ __forceinline__ uint32_t tf32_rna(float x) { return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u; }
 
 __device__ __forceinline__ float tc_tanh(float x) {
     float e, r;
