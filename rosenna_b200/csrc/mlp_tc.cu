@@ -429,20 +429,30 @@ __device__ __forceinline__ void tail_dots(float (&o)[NP], const float (&acc)[128
 #pragma unroll
     for (int q = 0; q < 8; q++) {
         if (128 * g + 16 * q >= np_prev) break;
+        // four K-rows at a time: their weight loads are issued back to back,
+        // then their FMAs (one load's latency per four rows, few registers)
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-            const float x = tc_act<ACT>(acc[16 * q + e]);
-            const uint32_t w_row = w_base + (uint32_t)((16 * q + e) * kTcTailMaxN * 4);
+        for (int e0 = 0; e0 < 16; e0 += 4) {
+            float4 w4[4][NP / 4];
 #pragma unroll
-            for (int n4 = 0; n4 < NP / 4; n4++) {
-                float4 w4;
-                asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                             : "=f"(w4.x), "=f"(w4.y), "=f"(w4.z), "=f"(w4.w)
-                             : "r"(w_row + 16u * n4));
-                o[4 * n4 + 0] = fmaf(x, w4.x, o[4 * n4 + 0]);
-                o[4 * n4 + 1] = fmaf(x, w4.y, o[4 * n4 + 1]);
-                o[4 * n4 + 2] = fmaf(x, w4.z, o[4 * n4 + 2]);
-                o[4 * n4 + 3] = fmaf(x, w4.w, o[4 * n4 + 3]);
+            for (int e = 0; e < 4; e++) {
+                const uint32_t w_row = w_base + (uint32_t)((16 * q + e0 + e) * kTcTailMaxN * 4);
+#pragma unroll
+                for (int n4 = 0; n4 < NP / 4; n4++)
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(w4[e][n4].x), "=f"(w4[e][n4].y), "=f"(w4[e][n4].z), "=f"(w4[e][n4].w)
+                                 : "r"(w_row + 16u * n4));
+            }
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float x = tc_act<ACT>(acc[16 * q + e0 + e]);
+#pragma unroll
+                for (int n4 = 0; n4 < NP / 4; n4++) {
+                    o[4 * n4 + 0] = fmaf(x, w4[e][n4].x, o[4 * n4 + 0]);
+                    o[4 * n4 + 1] = fmaf(x, w4[e][n4].y, o[4 * n4 + 1]);
+                    o[4 * n4 + 2] = fmaf(x, w4[e][n4].z, o[4 * n4 + 2]);
+                    o[4 * n4 + 3] = fmaf(x, w4[e][n4].w, o[4 * n4 + 3]);
+                }
             }
         }
     }
