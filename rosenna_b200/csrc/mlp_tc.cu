@@ -45,8 +45,6 @@ namespace {
 constexpr int kBM = 128;                 // samples per tile (UMMA M)
 constexpr int kKC = 32;                  // K per chunk: 32 fp32 = one 128-byte swizzle row
 constexpr int kNMax = 256;               // widest layer (UMMA N)
-constexpr int kThreadsTc = 256;           // lstm_tc_kernel: two groups of four warps (up to 255 registers)
-constexpr int kStagers = 6 * 32;          // lstm_tc_kernel: threads that stage A (all but the issuers' warps)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTCol = 0;             // TMEM cols [0,256): previous layer's activations
 constexpr uint32_t kPCol = 256;           // TMEM cols [256,512): partial sums of column half h at 256+128h
@@ -868,16 +866,10 @@ __device__ __forceinline__ void lstm_load_b(const TcLstmArgs &p, uint8_t *b0, ui
     tma_load_2d(b0 + s * 2 * kBTile + kBTile, &p.map, &b_full[s], q * kKC, p.Np);
 }
 
-// MMAs of half g for chunk jj (chunk q of its step), as issue_chunk / issue_in_turn.
-__device__ __forceinline__ bool lstm_issue(const TcLstmArgs &p, uint8_t *a0, uint8_t *b0, uint64_t *b_full,
-                                           uint64_t *a_full, uint64_t *a_empty, uint64_t *p_full, uint64_t *p_empty,
-                                           uint64_t *turn, uint32_t tmem, int g, int q, uint32_t jj, uint32_t &pi) {
-    const int s = jj & 1;
-    if (g == 1 && !mbar_wait(&turn[jj & 1], (jj >> 1) & 1, p.err, 8, q, (int)jj, 0, 0)) return false;
-    if (!mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, q, (int)jj, g, 0)) return false;
-    if (!mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, q, (int)jj, g, 0)) return false;
-    if (!mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, q, (int)pi, (int)jj, 0)) return false;
-    tc_fence_after();
+// The MMAs of group g's gate columns for the ring stage s, as mlp_tc_kernel's
+// issue_half.
+__device__ __forceinline__ void lstm_issue_half(const TcLstmArgs &p, uint8_t *a0, uint8_t *b0, uint32_t tmem, int g,
+                                                int s) {
     const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
     const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
     const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;
@@ -896,14 +888,11 @@ __device__ __forceinline__ bool lstm_issue(const TcLstmArgs &p, uint8_t *a0, uin
         const uint64_t adv = (uint64_t)((kk * 32) >> 4);
         umma_tf32(d, ah + adv, bh + adv, idesc, 1);
     }
-    umma_commit(&p_full[g]);
-    umma_commit(&a_empty[s]);
-    pi++;
-    if (g == 0) mbar_arrive(&turn[jj & 1]);
-    return true;
 }
 
-__global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_constant__ TcLstmArgs p) {
+// Warp roles as in mlp_tc_kernel: warps 0-7 the two column groups (drain,
+// stage, cell update), warp 8 lane 0 the MMA issuer, warp 9 lane 0 the B loader.
+__global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_constant__ TcLstmArgs p) {
     extern __shared__ uint8_t sm_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *const b0 = base;
@@ -913,37 +902,28 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
     uint64_t *const bars = reinterpret_cast<uint64_t *>(base + kSmemB + kSmemA + kLstmBias + kLstmXBuf);
     uint64_t *const b_full = bars, *const a_full = bars + 2, *const a_empty = bars + 4;
     uint64_t *const p_full = bars + 6, *const p_empty = bars + 8, *const t_ready = bars + 10;
-    uint64_t *const turn = bars + 16;
+    uint64_t *const mma_done = bars + 11;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = warp >> 2, quad = warp & 3;
-    const int r = quad * 32 + lane;
-    const bool issuer = lane == 0 && (warp == 0 || warp == 5);
-    const int halves = (warp == 0 || warp == 5) ? 0 : (warp == 1 || warp == 4) ? 3 : 1 << g;
-    const bool loader = warp == 2 && lane == 0;
-    const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;
     const int nch = p.nx + p.nh, T = p.T;
     const int ntiles = (int)((p.n + kBM - 1) / kBM);
-    const bool has_half = 128 * g < p.Np;
-    // the next step's x through the prefetch buffer (x parts of up to two chunks)
-    float *const xbuf = (halves && p.nx <= kLstmMaxNxPrefetch) ? xbuf_all : nullptr;
     // chunks of this CTA: its tiles x T steps x nch
     const long long my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const long long total = my_tiles * T * nch;
 
-    for (int i = tid; i < kNMax; i += kThreadsTc) sbias[i] = i < p.Np ? p.arena[p.b_off + i] : 0.f;
+    for (int i = tid; i < kNMax; i += kThreadsWs) sbias[i] = i < p.Np ? p.arena[p.b_off + i] : 0.f;
     static_assert(kNMax * 4 <= kLstmBias, "bias area");
     if (tid == 0) {
         for (int s = 0; s < 2; s++) {
             mbar_init(&b_full[s], 1);
-            mbar_init(&a_full[s], kStagers);
-            mbar_init(&a_empty[s], 2);
+            mbar_init(&a_full[s], 256);  // every group thread stages a K half of each chunk
+            mbar_init(&a_empty[s], 1);
             mbar_init(&p_full[s], 1);
             mbar_init(&p_empty[s], kBM);
-            mbar_init(&turn[s], 1);
         }
-        mbar_init(t_ready, kThreadsTc);
+        mbar_init(t_ready, 256);
+        mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -955,176 +935,193 @@ __global__ void __launch_bounds__(kThreadsTc, 1) lstm_tc_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
 
-    uint32_t b_issued = 0, b_done = 0;
-    if (loader) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(&p.map) : "memory");
-        for (long long q = 0; q < 2 && q < total; q++) lstm_load_b(p, b0, b_full, (int)(q % nch), b_issued++);
-    }
-
-    uint32_t j = 0, pu = 0, pi = 0, tb = 0;
-    bool ok = true;
-    float acc[128];
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const long long row = (long long)t * kBM + r;
-        const bool valid = row < p.n;
-        // the initial state: h0 into T columns 32g.., c0 into T columns 128+32g..
-        if (has_half) {
-#pragma unroll
-            for (int hf = 0; hf < 2; hf++) {
-                float hv[16], cv[16];
-#pragma unroll
-                for (int e = 0; e < 16; e++) {
-                    const int unit = 32 * g + 16 * hf + e;
-                    float h0 = 0.f, c0 = 0.f;
-                    if (unit < p.H && valid) {
-                        h0 = p.h0 ? p.h0[(long long)unit * p.ld_h0 + row]
-                                  : (p.h0_const >= 0 ? p.arena[p.h0_const + unit] : 0.f);
-                        c0 = p.c0 ? p.c0[(long long)unit * p.ld_c0 + row]
-                                  : (p.c0_const >= 0 ? p.arena[p.c0_const + unit] : 0.f);
-                    }
-                    hv[e] = h0;
-                    cv[e] = c0;
-                }
-                tmem_st16(lane_base + kTCol + (uint32_t)(32 * g + 16 * hf), hv);
-                tmem_st16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
-            }
-        }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        tc_fence_before();
-        mbar_arrive(t_ready);
-        ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, 0, (int)tb, (int)j, slot));
-        tb++;
-        tc_fence_after();
-        if (!ok) break;
-        // step 0: chunks 0 and 1 staged here, chunk 0 issued; later steps had
-        // theirs staged (and chunk 0 issued) during the step before
-        if (halves) {
-            lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 0, j, nullptr);
-            if (nch > 1) lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 1, j + 1, nullptr);
-        }
-        if (has_half && issuer) ok = lstm_issue(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g, 0, j, pi);
-        ok = __all_sync(0xffffffffu, ok);
-        for (int st = 0; st < T && ok; st++) {
-            // x of the next step: its chunks are staged at this step's last iterations
-            if (xbuf && st + 1 < T) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
-            if (has_half) {
-                const uint32_t b_addr = smem_u32(sbias + 128 * g);
-#pragma unroll
-                for (int q = 0; q < 32; q++)
-                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                                 : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
-                                 : "r"(b_addr + 16u * q));
-            }
-            for (int c = 0; c < nch && ok; c++) {
-                const uint32_t jj = j + (uint32_t)c;
-                const int s = jj & 1;
-                if (has_half) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (st << 8) | c, (int)pu,
-                                                           (int)jj, slot));
+    if (warp >= 8) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+        if (warp == 8 && lane == 0) {
+            // ---- MMA issuer: chunk by chunk, group 0's gates then group 1's ----
+            uint32_t pi0 = 0, pi1 = 0;
+            bool ok = true;
+            for (long long q = 0; q < total && ok; q++) {
+                const uint32_t jj = (uint32_t)q;
+                const int s = jj & 1, c = (int)(q % nch);
+                ok = mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, c, (int)jj, 0, 2) &&
+                     mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, c, (int)jj, 0, 2);
+                for (int g = 0; g < 2 && ok; g++) {
+                    if (128 * g >= p.Np) continue;
+                    uint32_t &pi = g ? pi1 : pi0;
+                    ok = mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, c, (int)pi, (int)jj, 2);
                     if (!ok) break;
                     tc_fence_after();
+                    lstm_issue_half(p, a0, b0, tmem, g, s);
+                    umma_commit(&p_full[g]);
+                    pi++;
+                }
+                if (ok) umma_commit(&a_empty[s]);
+            }
+            umma_commit(mma_done);
+            mbar_wait(mma_done, 0, p.err, 0);
+        } else if (warp == 9 && lane == 0) {
+            // ---- B loader: two chunks ahead ----
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&p.map) : "memory");
+            uint32_t issued = 0;
+            for (long long q = 0; q < 2 && q < total; q++) lstm_load_b(p, b0, b_full, (int)(q % nch), issued++);
+            for (long long q = 0; q + 2 < total; q++) {
+                const uint32_t jj = (uint32_t)q;
+                if (!mbar_wait(&a_empty[jj & 1], (jj >> 1) & 1, p.err, 5, (int)(q % nch), (int)jj, (int)issued, 1)) break;
+                lstm_load_b(p, b0, b_full, (int)((q + 2) % nch), issued++);
+            }
+            for (uint32_t k = issued > 2 ? issued - 2 : 0; k < issued; k++)
+                mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
+        }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
+        const int g = warp >> 2, quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        const int halves = 1 << g;
+        const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;
+        const bool has_half = 128 * g < p.Np;
+        // the next step's x through the prefetch buffer (x parts of up to two chunks)
+        float *const xbuf = p.nx <= kLstmMaxNxPrefetch ? xbuf_all : nullptr;
+        uint32_t j = 0, pu = 0, tb = 0;
+        bool ok = true;
+        float acc[128];
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const long long row = (long long)t * kBM + r;
+            const bool valid = row < p.n;
+            // the initial state: h0 into T columns 32g.., c0 into T columns 128+32g..
+            if (has_half) {
 #pragma unroll
-                    for (int q0 = 0; q0 < 8; q0 += 4) {
-                        if (128 * g + 16 * q0 < p.Np) {
-                            uint32_t v[4][16];
+                for (int hf = 0; hf < 2; hf++) {
+                    float hv[16], cv[16];
 #pragma unroll
-                            for (int u = 0; u < 4; u++)
-                                if (128 * g + 16 * (q0 + u) < p.Np)
-                                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int u = 0; u < 4; u++)
-                                if (128 * g + 16 * (q0 + u) < p.Np) {
-#pragma unroll
-                                    for (int e = 0; e < 16; e += 2)
-                                        add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e], v[u][e + 1]);
-                                }
+                    for (int e = 0; e < 16; e++) {
+                        const int unit = 32 * g + 16 * hf + e;
+                        float h0 = 0.f, c0 = 0.f;
+                        if (unit < p.H && valid) {
+                            h0 = p.h0 ? p.h0[(long long)unit * p.ld_h0 + row]
+                                      : (p.h0_const >= 0 ? p.arena[p.h0_const + unit] : 0.f);
+                            c0 = p.c0 ? p.c0[(long long)unit * p.ld_c0 + row]
+                                      : (p.c0_const >= 0 ? p.arena[p.c0_const + unit] : 0.f);
                         }
+                        hv[e] = h0;
+                        cv[e] = c0;
                     }
-                    tc_fence_before();
-                    mbar_arrive(&p_empty[g]);
-                    pu++;
-                    // the next chunk goes in at once: this step's, or the next step's first (x)
-                    if (issuer && (c + 1 < nch || st + 1 < T))
-                        ok = lstm_issue(p, a0, b0, b_full, a_full, a_empty, p_full, p_empty, turn, tmem, g,
-                                        c + 1 < nch ? c + 1 : 0, jj + 1, pi);
-                    ok = __all_sync(0xffffffffu, ok);
+                    tmem_st16(lane_base + kTCol + (uint32_t)(32 * g + 16 * hf), hv);
+                    tmem_st16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
+                }
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(t_ready);
+            ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, 0, (int)tb, (int)j, slot));
+            tb++;
+            tc_fence_after();
+            if (!ok) break;
+            // step 0: chunks 0 and 1 staged here; later steps had theirs staged during
+            // the step before
+            lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 0, j, nullptr);
+            if (nch > 1) lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 1, j + 1, nullptr);
+            for (int st = 0; st < T && ok; st++) {
+                // x of the next step: its chunks are staged at this step's last iterations
+                if (xbuf && st + 1 < T) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
+                if (has_half) {
+                    const uint32_t b_addr = smem_u32(sbias + 128 * g);
+#pragma unroll
+                    for (int q = 0; q < 32; q++)
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
+                                     : "r"(b_addr + 16u * q));
+                }
+                for (int c = 0; c < nch && ok; c++) {
+                    const uint32_t jj = j + (uint32_t)c;
+                    const int s = jj & 1;
+                    if (has_half) {
+                        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (st << 8) | c, (int)pu,
+                                                               (int)jj, slot));
+                        if (!ok) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int q0 = 0; q0 < 8; q0 += 4) {
+                            if (128 * g + 16 * q0 < p.Np) {
+                                uint32_t v[4][16];
+#pragma unroll
+                                for (int u = 0; u < 4; u++)
+                                    if (128 * g + 16 * (q0 + u) < p.Np)
+                                        tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int u = 0; u < 4; u++)
+                                    if (128 * g + 16 * (q0 + u) < p.Np) {
+#pragma unroll
+                                        for (int e = 0; e < 16; e += 2)
+                                            add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e],
+                                                 v[u][e + 1]);
+                                    }
+                            }
+                        }
+                        tc_fence_before();
+                        mbar_arrive(&p_empty[g]);
+                        pu++;
+                    }
+                    ok = __all_sync(0xffffffffu, mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (st << 8) | c,
+                                                           (int)jj, (int)pu, slot));
                     if (!ok) break;
-                } else if (issuer) {
-                    ok = mbar_wait(&turn[jj & 1], (jj >> 1) & 1, p.err, 8, c, (int)jj, 0, 0);
-                    umma_commit(&a_empty[s]);
-                }
-                ok = __all_sync(0xffffffffu, ok &&
-                                mbar_wait(&a_empty[s], (jj >> 1) & 1, p.err, 5, (st << 8) | c, (int)jj, (int)pu, slot));
-                if (!ok) break;
-                if (loader) {
-                    b_done = jj + 1;
-                    const long long q2 = (long long)jj + 2 - 0;  // chunk index of this CTA's stream
-                    if (q2 < total) lstm_load_b(p, b0, b_full, (int)(q2 % nch), b_issued++);
-                }
-                // stage chunk c+2: of this step, or an x chunk of the next step (an h
-                // chunk of the next step waits for this step's cell update)
-                if (halves) {
+                    // stage chunk c+2: of this step, or an x chunk of the next step (an h
+                    // chunk of the next step waits for this step's cell update)
                     const int q2 = c + 2;
                     if (q2 < nch) lstm_stage(p, a0, a_full, lane_base, r, halves, t, st, q2, jj + 2, xbuf);
                     else if (st + 1 < T && q2 - nch < p.nx)
                         lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, q2 - nch, jj + 2, xbuf);
                 }
-            }
-            j += (uint32_t)nch;
-            if (!ok) break;
-            // cell update (layers.f90 lstm_cell): gates of unit u at acc[4u..4u+3]
-            if (has_half) {
+                j += (uint32_t)nch;
+                if (!ok) break;
+                // cell update (layers.f90 lstm_cell): gates of unit u at acc[4u..4u+3]
+                if (has_half) {
 #pragma unroll
-                for (int hf = 0; hf < 2; hf++) {
-                    float cv[16], hv[16];
-                    tmem_ld16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const int u = 16 * hf + e;
-                        const float ig = tc_act<3>(acc[4 * u]), fg = tc_act<3>(acc[4 * u + 1]);
-                        const float gg = tc_act<2>(acc[4 * u + 2]), og = tc_act<3>(acc[4 * u + 3]);
-                        cv[e] = fg * cv[e] + ig * gg;
-                        hv[e] = og * tc_act<2>(cv[e]);
-                    }
-                    tmem_st16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
-                    tmem_st16(lane_base + kTCol + (uint32_t)(32 * g + 16 * hf), hv);
-                    if (valid) {
+                    for (int hf = 0; hf < 2; hf++) {
+                        float cv[16], hv[16];
+                        tmem_ld16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
 #pragma unroll
                         for (int e = 0; e < 16; e++) {
-                            const int unit = 32 * g + 16 * hf + e;
-                            if (unit < p.H) {
-                                if (p.y) p.y[(long long)(st + (long long)T * unit) * p.ld_y + row] = hv[e];
-                                if (st + 1 == T) {
-                                    if (p.hn) p.hn[(long long)unit * p.ld_hn + row] = hv[e];
-                                    if (p.cn) p.cn[(long long)unit * p.ld_cn + row] = cv[e];
+                            const int u = 16 * hf + e;
+                            const float ig = tc_act<3>(acc[4 * u]), fg = tc_act<3>(acc[4 * u + 1]);
+                            const float gg = tc_act<2>(acc[4 * u + 2]), og = tc_act<3>(acc[4 * u + 3]);
+                            cv[e] = fg * cv[e] + ig * gg;
+                            hv[e] = og * tc_act<2>(cv[e]);
+                        }
+                        tmem_st16(lane_base + kTCol + (uint32_t)(128 + 32 * g + 16 * hf), cv);
+                        tmem_st16(lane_base + kTCol + (uint32_t)(32 * g + 16 * hf), hv);
+                        if (valid) {
+#pragma unroll
+                            for (int e = 0; e < 16; e++) {
+                                const int unit = 32 * g + 16 * hf + e;
+                                if (unit < p.H) {
+                                    if (p.y) p.y[(long long)(st + (long long)T * unit) * p.ld_y + row] = hv[e];
+                                    if (st + 1 == T) {
+                                        if (p.hn) p.hn[(long long)unit * p.ld_hn + row] = hv[e];
+                                        if (p.cn) p.cn[(long long)unit * p.ld_cn + row] = cv[e];
+                                    }
                                 }
                             }
                         }
                     }
                 }
+                // h_t in T for the next step (both groups' units feed both groups' MMAs)
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                mbar_arrive(t_ready);
+                ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, st, (int)tb, (int)j, slot));
+                tb++;
+                tc_fence_after();
+                if (!ok) break;
+                // the next step's chunk 1 when it is an h chunk (nx == 1)
+                if (st + 1 < T && nch > 1 && p.nx == 1)
+                    lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, 1, j + 1, xbuf);
             }
-            // h_t in T for the next step (both groups' units feed both groups' MMAs)
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            tc_fence_before();
-            mbar_arrive(t_ready);
-            ok = __all_sync(0xffffffffu, mbar_wait(t_ready, tb & 1, p.err, 7, st, (int)tb, (int)j, slot));
-            tb++;
-            tc_fence_after();
-            if (!ok) break;
-            // the next step's chunk 1 when it is an h chunk (nx == 1)
-            if (halves && st + 1 < T && nch > 1 && p.nx == 1)
-                lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, 1, j + 1, xbuf);
         }
     }
-    if (issuer) {
-        umma_commit(&p_full[g]);
-        for (uint32_t k = pu; k <= pi; k++) mbar_wait(&p_full[g], k & 1, p.err, 0);
-    }
-    if (loader)
-        for (uint32_t k = b_done; k < b_issued; k++) mbar_wait(&b_full[k & 1], (k >> 1) & 1, p.err, 0);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -1149,7 +1146,12 @@ cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st) {
     const long long tiles = (a.n + kBM - 1) / kBM;
     const int grid = (int)(tiles < num_sms ? tiles : num_sms);
     if (grid <= 0) return cudaSuccess;
-    lstm_tc_kernel<<<grid, kThreadsTc, lstm_tc_smem(), st>>>(a);
+    static const int regs = [] {
+        cudaFuncAttributes fa{};
+        return cudaFuncGetAttributes(&fa, lstm_tc_kernel) == cudaSuccess ? fa.numRegs : -1;
+    }();
+    if (regs != kLaunchRegs) return cudaErrorInvalidConfiguration;  // the setmaxnreg split needs exactly these
+    lstm_tc_kernel<<<grid, kThreadsWs, lstm_tc_smem(), st>>>(a);
     return cudaGetLastError();
 }
 
