@@ -35,7 +35,7 @@ sys.path.insert(0, ROOT)
 # DRAM bytes (read + write) per sample of the dominant kernel, from the
 # committed ncu captures (profiles/); scaled by the batch for `traffic`
 NCU_TRAFFIC_PER_SAMPLE = {
-    ("wide_mlp", "mlp_tc_kernel"): (69.478144e6 + 9.841664e6) / 1048576,
+    ("wide_mlp", "mlp_tc_kernel"): (69.486592e6 + 10.319616e6) / 1048576,
 }
 
 DEFAULT_WORKLOAD = "wide_mlp"
