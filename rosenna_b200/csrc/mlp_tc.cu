@@ -867,9 +867,9 @@ __device__ __forceinline__ void lstm_load_b(const TcLstmArgs &p, uint8_t *b0, ui
 }
 
 // The MMAs of group g's gate columns for the ring stage s, as mlp_tc_kernel's
-// issue_half.
+// issue_half; `first`: the chunk starts its partial (else it accumulates).
 __device__ __forceinline__ void lstm_issue_half(const TcLstmArgs &p, uint8_t *a0, uint8_t *b0, uint32_t tmem, int g,
-                                                int s) {
+                                                int s, bool first) {
     const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile));
     const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + s * 2 * kATile + kATile));
     const uint64_t boff = (uint64_t)(g * 128 * 128) >> 4;
@@ -880,7 +880,7 @@ __device__ __forceinline__ void lstm_issue_half(const TcLstmArgs &p, uint8_t *a0
 #pragma unroll
     for (int kk = 0; kk < kKC / 8; kk++) {
         const uint64_t adv = (uint64_t)((kk * 32) >> 4);
-        umma_tf32(d, al + adv, bh + adv, idesc, kk);
+        umma_tf32(d, al + adv, bh + adv, idesc, (kk > 0 || !first) ? 1u : 0u);
         umma_tf32(d, ah + adv, bl + adv, idesc, 1);
     }
 #pragma unroll
@@ -939,23 +939,27 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
     if (warp >= 8) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
         if (warp == 8 && lane == 0) {
-            // ---- MMA issuer: chunk by chunk, group 0's gates then group 1's ----
+            // ---- MMA issuer: chunk by chunk, group 0's gates then group 1's; a
+            // step's x chunks accumulate into one partial, its h chunks into another ----
             uint32_t pi0 = 0, pi1 = 0;
             bool ok = true;
             for (long long q = 0; q < total && ok; q++) {
                 const uint32_t jj = (uint32_t)q;
                 const int s = jj & 1, c = (int)(q % nch);
+                const bool first = c == 0 || c == p.nx, part_end = c == p.nx - 1 || c == nch - 1;
                 ok = mbar_wait(&b_full[s], (jj >> 1) & 1, p.err, 2, c, (int)jj, 0, 2) &&
                      mbar_wait(&a_full[s], (jj >> 1) & 1, p.err, 3, c, (int)jj, 0, 2);
                 for (int g = 0; g < 2 && ok; g++) {
                     if (128 * g >= p.Np) continue;
                     uint32_t &pi = g ? pi1 : pi0;
-                    ok = mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, c, (int)pi, (int)jj, 2);
+                    if (first) ok = mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, c, (int)pi, (int)jj, 2);
                     if (!ok) break;
                     tc_fence_after();
-                    lstm_issue_half(p, a0, b0, tmem, g, s);
-                    umma_commit(&p_full[g]);
-                    pi++;
+                    lstm_issue_half(p, a0, b0, tmem, g, s, first);
+                    if (part_end) {
+                        umma_commit(&p_full[g]);
+                        pi++;
+                    }
                 }
                 if (ok) umma_commit(&a_empty[s]);
             }
@@ -1024,8 +1028,6 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
             lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 0, j, nullptr);
             if (nch > 1) lstm_stage(p, a0, a_full, lane_base, r, halves, t, 0, 1, j + 1, nullptr);
             for (int st = 0; st < T && ok; st++) {
-                // x of the next step: its chunks are staged at this step's last iterations
-                if (xbuf && st + 1 < T) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
                 if (has_half) {
                     const uint32_t b_addr = smem_u32(sbias + 128 * g);
 #pragma unroll
@@ -1037,7 +1039,9 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
                 for (int c = 0; c < nch && ok; c++) {
                     const uint32_t jj = j + (uint32_t)c;
                     const int s = jj & 1;
-                    if (has_half) {
+                    // the x part of the gates is one partial, the h part another (the
+                    // truncating TMEM accumulation over 64 K stays ~1e-7 here: small gates)
+                    if (has_half && (c == p.nx - 1 || c == nch - 1)) {
                         ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (st << 8) | c, (int)pu,
                                                                (int)jj, slot));
                         if (!ok) break;
@@ -1074,6 +1078,9 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
                     if (q2 < nch) lstm_stage(p, a0, a_full, lane_base, r, halves, t, st, q2, jj + 2, xbuf);
                     else if (st + 1 < T && q2 - nch < p.nx)
                         lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, q2 - nch, jj + 2, xbuf);
+                    // x of the next step, while the h MMAs run (after the staging the issuer
+                    // waits for): its chunks are staged at this step's last iterations
+                    if (c == p.nx - 1 && xbuf && st + 1 < T) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
                 }
                 j += (uint32_t)nch;
                 if (!ok) break;
