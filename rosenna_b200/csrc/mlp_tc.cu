@@ -1073,14 +1073,17 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
                                                            (int)jj, (int)pu, slot));
                     if (!ok) break;
                     // stage chunk c+2: of this step, or an x chunk of the next step (an h
-                    // chunk of the next step waits for this step's cell update)
+                    // chunk of the next step waits for this step's cell update).  The next
+                    // step's x is prefetched at c = nx-1, after this iteration's staging so
+                    // that it runs beside the h MMAs -- unless this iteration already stages
+                    // the next step's x (two-chunk steps)
                     const int q2 = c + 2;
+                    const bool prefetch = c == p.nx - 1 && xbuf && st + 1 < T;
+                    if (prefetch && q2 >= nch) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
                     if (q2 < nch) lstm_stage(p, a0, a_full, lane_base, r, halves, t, st, q2, jj + 2, xbuf);
                     else if (st + 1 < T && q2 - nch < p.nx)
                         lstm_stage(p, a0, a_full, lane_base, r, halves, t, st + 1, q2 - nch, jj + 2, xbuf);
-                    // x of the next step, while the h MMAs run (after the staging the issuer
-                    // waits for): its chunks are staged at this step's last iterations
-                    if (c == p.nx - 1 && xbuf && st + 1 < T) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
+                    if (prefetch && q2 < nch) lstm_prefetch_x(p, xbuf, r, halves, t, st + 1);
                 }
                 j += (uint32_t)nch;
                 if (!ok) break;
