@@ -1145,6 +1145,16 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
 
 size_t mlp_tc_smem_bytes() { return 1024 + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX + kSmemBars; }
 
+bool tc_register_split_ok() {
+    cudaFuncAttributes a{}, b{};
+    if (cudaFuncGetAttributes(&a, mlp_tc_kernel) != cudaSuccess ||
+        cudaFuncGetAttributes(&b, lstm_tc_kernel) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return true;
+    }
+    return a.numRegs == kLaunchRegs && b.numRegs == kLaunchRegs;
+}
+
 cudaError_t mlp_tc_configure() {
     cudaError_t e =
         cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());

@@ -62,6 +62,11 @@ struct TcLstmArgs {
 };
 
 size_t mlp_tc_smem_bytes();
+// The tensor-core kernels redistribute their launch registers between roles
+// (setmaxnreg) and only run when the compiler gave them exactly the count that
+// split assumes.  False when it did not (the plan then uses the FFMA kernels);
+// true also when no device can be asked (launches check again).
+bool tc_register_split_ok();
 cudaError_t mlp_tc_configure();
 cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st);
 cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);

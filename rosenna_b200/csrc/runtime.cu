@@ -432,6 +432,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
     }
     // tensor-core path for MLP chains with a layer >= 128 wide and all <= 256
     // (ROSENNA_MLP_PATH=ffma forces the FFMA kernel, =tc any eligible chain)
+    const bool tc_ok = tc_register_split_ok();
     const char *path = getenv("ROSENNA_MLP_PATH");
     const std::string mlp_path = path ? path : "";
     for (auto &s : P.steps) {
@@ -442,7 +443,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             eligible = eligible && l.tc_w_off >= 0;
             widest = std::max(widest, l.M);
         }
-        s.tc = eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 128);
+        s.tc = tc_ok && eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 128);
     }
     // tensor-core LSTM for 128 < 4H <= 256, both column halves busy (with 4H <= 128
     // one half idles and the per-step chain is latency-bound: the FFMA kernel is
@@ -451,7 +452,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
     const std::string lstm_path = lpath ? lpath : "";
     for (auto &s : P.steps)
         if (s.kind == Step::LSTM)
-            s.tc = lstm_path != "ffma" && s.lstm_tc_w_off >= 0 && (lstm_path == "tc" || 4 * s.H > 128);
+            s.tc = tc_ok && lstm_path != "ffma" && s.lstm_tc_w_off >= 0 && (lstm_path == "tc" || 4 * s.H > 128);
     g_ctx.is_io_in.assign(P.buf_rows.size(), false);
     g_ctx.is_io_out.assign(P.buf_rows.size(), false);
     for (auto &io : P.inputs) g_ctx.is_io_in[(size_t)io.buf] = true;
