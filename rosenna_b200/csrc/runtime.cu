@@ -430,8 +430,10 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         if (s.kind == Step::LSTM && !lstm_smem_bytes(s.Ip, s.Hp, &S))
             return Status::Err(ROSENNA_ERR_UNSUPPORTED, "LSTM hidden size too large for the on-chip kernel");
     }
-    // tensor-core path for MLP chains with a layer >= 128 wide and all <= 256
-    // (ROSENNA_MLP_PATH=ffma forces the FFMA kernel, =tc any eligible chain)
+    // tensor-core path for MLP chains with a layer >= 64 wide and all <= 256
+    // (measured: the 10-64-64-64-5 chain runs 42 % faster there than on the FFMA
+    // kernel; chains a few units wide stay on FFMA); ROSENNA_MLP_PATH=ffma forces
+    // the FFMA kernel, =tc any eligible chain
     const bool tc_ok = tc_register_split_ok();
     const char *path = getenv("ROSENNA_MLP_PATH");
     const std::string mlp_path = path ? path : "";
@@ -443,7 +445,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             eligible = eligible && l.tc_w_off >= 0;
             widest = std::max(widest, l.M);
         }
-        s.tc = tc_ok && eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 128);
+        s.tc = tc_ok && eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 64);
     }
     // tensor-core LSTM for 128 < 4H <= 256, both column halves busy (with 4H <= 128
     // one half idles and the per-step chain is latency-bound: the FFMA kernel is
