@@ -427,13 +427,14 @@ __device__ __forceinline__ void tail_dots(float (&o)[NP], const float (&acc)[128
 #pragma unroll
     for (int q = 0; q < 8; q++) {
         if (128 * g + 16 * q >= np_prev) break;
-        // four K-rows at a time: their weight loads are issued back to back,
-        // then their FMAs (one load's latency per four rows, few registers)
+        // RB K-rows at a time (32 weight registers): their weight loads are issued
+        // back to back, then their FMAs (one load's latency per RB rows)
+        constexpr int RB = NP <= 8 ? 4 : 2;
 #pragma unroll
-        for (int e0 = 0; e0 < 16; e0 += 4) {
-            float4 w4[4][NP / 4];
+        for (int e0 = 0; e0 < 16; e0 += RB) {
+            float4 w4[RB][NP / 4];
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
+            for (int e = 0; e < RB; e++) {
                 const uint32_t w_row = w_base + (uint32_t)((16 * q + e0 + e) * kTcTailMaxN * 4);
 #pragma unroll
                 for (int n4 = 0; n4 < NP / 4; n4++)
@@ -442,7 +443,7 @@ __device__ __forceinline__ void tail_dots(float (&o)[NP], const float (&acc)[128
                                  : "r"(w_row + 16u * n4));
             }
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
+            for (int e = 0; e < RB; e++) {
                 const float x = tc_act<ACT>(acc[16 * q + e0 + e]);
 #pragma unroll
                 for (int n4 = 0; n4 < NP / 4; n4++) {
@@ -772,6 +773,329 @@ __global__ void __launch_bounds__(kThreadsWs, 1) mlp_tc_kernel(const __grid_cons
                         tc_fence_before();
                         mbar_arrive(t_ready);
                     }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// ============================================================================
+// Chains no wider than 128 (every layer's Np <= 128): in mlp_tc_kernel one
+// column group would hold all the columns while the other idled, and a tile's
+// layer ends and tail would stall the tensor pipe.  Here each group takes a
+// tile of its own (group g the tiles blockIdx.x + (2k+g)*gridDim.x) with its
+// own 2-slot A ring, its own TMEM partial buffer and T region (columns
+// 128g..128g+127); the B ring is shared, one stage per chunk position (the
+// same weights serve both tiles).  The issuer takes chunk c of layer l for
+// group 0's tile, then for group 1's, so one group's layer end overlaps the
+// other group's MMAs.  Each thread stages and reads only its own sample row,
+// so the groups never wait for one another (only on the shared B ring).
+// ============================================================================
+constexpr uint32_t kDualBTile = 128 * 128;            // Np <= 128 rows of 128 bytes
+constexpr uint32_t kDualSmemB = 2 * 2 * kDualBTile;  // 2 stages x (hi, lo)
+constexpr uint32_t kDualSmemA = 2 * 2 * 2 * kATile;  // 2 groups x 2 slots x (hi, lo)
+constexpr uint32_t kDualSmemBias = (kTcMaxLayers + 1) * 128 * 4;  // per layer, then the tail's
+constexpr uint32_t kDualSmemTailW = 128 * kTcTailMaxN * 4;
+size_t mlp_tc_dual_smem() { return 1024 + kDualSmemB + kDualSmemA + kDualSmemBias + kDualSmemTailW + kSmemBars; }
+
+// (pair k, layer l, chunk c) after `steps` chunk positions in this CTA's order
+__device__ __forceinline__ bool pair_after(const TcArgs &p, int npairs, int &k, int &l, int &c, int steps) {
+    c += steps;
+    while (c >= p.L[l].nch) {
+        c -= p.L[l].nch;
+        if (++l == p.nlayers) {
+            l = 0;
+            if (++k >= npairs) return false;
+        }
+    }
+    return true;
+}
+
+// One row of the CUDA-core tail: bias, activation, the outputs of `row` (the
+// activation switch outside the per-output loop keeps the registers down).
+template <int NP, int ACT>
+__device__ __forceinline__ void write_tail_row_act(const TcArgs &p, const float (&o)[NP], const float *btail,
+                                                   long long row) {
+#pragma unroll
+    for (int n = 0; n < NP; n++) {
+        if (n >= p.tail_n) break;
+        p.out[row + (long long)n * p.ld_out] = tc_act<ACT>(o[n] + btail[n]);
+    }
+}
+template <int NP>
+__device__ __forceinline__ void write_tail_row(const TcArgs &p, const float (&o)[NP], const float *btail, long long row) {
+    if (row >= p.n) return;
+    switch (p.tail_act) {
+        case 1: write_tail_row_act<NP, 1>(p, o, btail, row); break;
+        case 2: write_tail_row_act<NP, 2>(p, o, btail, row); break;
+        case 3: write_tail_row_act<NP, 3>(p, o, btail, row); break;
+        default: write_tail_row_act<NP, 0>(p, o, btail, row); break;
+    }
+}
+
+__device__ __forceinline__ void load_b_dual(const TcArgs &p, uint8_t *b0, uint64_t *b_full, int l, int c, uint32_t m) {
+    const int s = m & 1;
+    mbar_arrive_expect_tx(&b_full[s], 2u * (uint32_t)p.L[l].Np * 128u);
+    tma_load_2d(b0 + s * 2 * kDualBTile, &p.maps[l], &b_full[s], c * kKC, 0);
+    tma_load_2d(b0 + s * 2 * kDualBTile + kDualBTile, &p.maps[l], &b_full[s], c * kKC, p.L[l].Np);
+}
+
+__global__ void __launch_bounds__(kThreadsWs, 1) mlp_tc_dual_kernel(const __grid_constant__ TcArgs p) {
+    extern __shared__ uint8_t sm_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *const b0 = base;               // B stage s: hi at b0 + s*2*kDualBTile, lo + kDualBTile
+    uint8_t *const a0 = base + kDualSmemB;  // group g, slot s: hi at a0 + (2g+s)*2*kATile, lo + kATile
+    float *const sbias = reinterpret_cast<float *>(base + kDualSmemB + kDualSmemA);  // [l][128], tail at [nl]
+    float *const stail = reinterpret_cast<float *>(base + kDualSmemB + kDualSmemA + kDualSmemBias);
+    uint64_t *const bars =
+        reinterpret_cast<uint64_t *>(base + kDualSmemB + kDualSmemA + kDualSmemBias + kDualSmemTailW);
+    uint64_t *const b_full = bars, *const b_empty = bars + 2;
+    uint64_t *const a_full = bars + 4, *const a_empty = bars + 8;  // [group][slot]
+    uint64_t *const p_full = bars + 12, *const p_empty = bars + 14, *const mma_done = bars + 16;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 18);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nl = p.nlayers;
+    const int ntiles = (int)((p.n + kBM - 1) / kBM);
+    // tile pairs of this CTA: pair k holds tiles blockIdx.x + (2k + g) * gridDim.x
+    const int npairs = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (2 * (int)gridDim.x) + 1 : 0;
+
+    for (int i = tid; i < nl * 128; i += kThreadsWs) {
+        const int l = i / 128, j = i - l * 128;
+        sbias[i] = j < p.L[l].Np ? p.arena[p.L[l].b_off + j] : 0.f;
+    }
+    if (p.tail_n > 0) {  // zero beyond K and tail_np: those activations meet zero weights
+        for (int i = tid; i < 128 * kTcTailMaxN; i += kThreadsWs) {
+            const int k = i / kTcTailMaxN, n = i - k * kTcTailMaxN;
+            stail[i] = (k < p.tail_kp && n < p.tail_np) ? p.arena[p.tail_w_off + (long long)k * p.tail_np + n] : 0.f;
+        }
+        for (int i = tid; i < kTcTailMaxN; i += kThreadsWs)
+            sbias[nl * 128 + i] = i < p.tail_np ? p.arena[p.tail_b_off + i] : 0.f;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);     // one tcgen05.commit after both tiles' MMAs
+            mbar_init(&p_full[s], 1);
+            mbar_init(&p_empty[s], kBM);   // the group's 128 threads have drained the partial
+        }
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&a_full[i], kBM);    // the group's 128 threads have staged the chunk
+            mbar_init(&a_empty[i], 1);
+        }
+        mbar_init(mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp >= 8) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+        if (warp == 8 && lane == 0) {
+            // ---- MMA issuer: chunk (l, c) for group 0's tile, then for group 1's ----
+            uint32_t m = 0, jg0 = 0, jg1 = 0, pi0 = 0, pi1 = 0;
+            bool ok = true;
+            for (int k = 0; k < npairs && ok; k++) {
+                const int ng = (int)blockIdx.x + (2 * k + 1) * (int)gridDim.x < ntiles ? 2 : 1;
+                for (int l = 0; l < nl && ok; l++) {
+                    const int nch = p.L[l].nch;
+                    const uint32_t idesc = idesc_tf32(p.L[l].Np);
+                    for (int c = 0; c < nch && ok; c++, m++) {
+                        const int sb = m & 1;
+                        ok = mbar_wait(&b_full[sb], (m >> 1) & 1, p.err, 2, (l << 8) | c, (int)m, 0, 2);
+                        for (int g = 0; g < ng && ok; g++) {
+                            uint32_t &jg = g ? jg1 : jg0, &pi = g ? pi1 : pi0;
+                            const uint32_t sa = jg & 1;
+                            ok = mbar_wait(&a_full[2 * g + sa], (jg >> 1) & 1, p.err, 3, (l << 8) | c, (int)jg, g, 2) &&
+                                 mbar_wait(&p_empty[g], (pi & 1) ^ 1, p.err, 4, (l << 8) | c, (int)pi, g, 2);
+                            if (!ok) break;
+                            tc_fence_after();
+                            const uint64_t ah = desc_kmajor_sw128(smem_u32(a0 + (2 * g + sa) * 2 * kATile));
+                            const uint64_t al = desc_kmajor_sw128(smem_u32(a0 + (2 * g + sa) * 2 * kATile + kATile));
+                            const uint64_t bh = desc_kmajor_sw128(smem_u32(b0 + sb * 2 * kDualBTile));
+                            const uint64_t bl = desc_kmajor_sw128(smem_u32(b0 + sb * 2 * kDualBTile + kDualBTile));
+                            const uint32_t d = tmem + kPCol + (uint32_t)(128 * g);
+#pragma unroll
+                            for (int kk = 0; kk < kKC / 8; kk++) {
+                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+                                umma_tf32(d, al + adv, bh + adv, idesc, kk);
+                                umma_tf32(d, ah + adv, bl + adv, idesc, 1);
+                            }
+#pragma unroll
+                            for (int kk = 0; kk < kKC / 8; kk++) {
+                                const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+                                umma_tf32(d, ah + adv, bh + adv, idesc, 1);
+                            }
+                            umma_commit(&p_full[g]);
+                            umma_commit(&a_empty[2 * g + sa]);
+                            pi++;
+                            jg++;
+                        }
+                        if (ok) umma_commit(&b_empty[sb]);  // both tiles' MMAs of this B stage
+                    }
+                }
+            }
+            umma_commit(mma_done);
+            mbar_wait(mma_done, 0, p.err, 0);
+        } else if (warp == 9 && lane == 0) {
+            // ---- B loader: two chunk positions ahead ----
+            for (int l = 0; l < nl; l++) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.maps[l]) : "memory");
+            uint32_t issued = 0;
+            if (npairs > 0) {
+                load_b_dual(p, b0, b_full, 0, 0, issued++);
+                int k1 = 0, l1 = 0, c1 = 0;
+                if (pair_after(p, npairs, k1, l1, c1, 1)) load_b_dual(p, b0, b_full, l1, c1, issued++);
+                int k = 0, l = 0, c = 0;
+                uint32_t m = 0;
+                bool more = true;
+                while (more) {
+                    if (!mbar_wait(&b_empty[m & 1], (m >> 1) & 1, p.err, 5, (l << 8) | c, (int)m, (int)issued, 1))
+                        break;
+                    int k2 = k, l2 = l, c2 = c;
+                    if (pair_after(p, npairs, k2, l2, c2, 2)) load_b_dual(p, b0, b_full, l2, c2, issued++);
+                    m++;
+                    more = pair_after(p, npairs, k, l, c, 1);
+                }
+            }
+            // copies issued but not seen consumed (an error path) land first
+            for (uint32_t q = issued > 2 ? issued - 2 : 0; q < issued; q++)
+                mbar_wait(&b_full[q & 1], (q >> 1) & 1, p.err, 0);
+        }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
+        const int g = warp >> 2, quad = warp & 3;
+        const int r = quad * 32 + lane;  // sample row in the tile == TMEM lane
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        const uint32_t t_base = lane_base + 128u * g;  // this group's T columns (kTCol + 128g)
+        uint8_t *const ag = a0 + 2 * g * 2 * kATile;  // this group's two A slots
+        uint64_t *const af = a_full + 2 * g, *const ae = a_empty + 2 * g;
+        const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;
+        uint32_t j = 0, pu = 0;  // chunks of this group seen consumed; partials drained
+        bool ok = true;
+        float acc[128];
+        for (int k = 0; k < npairs && ok; k++) {
+            const int t = (int)blockIdx.x + (2 * k + g) * (int)gridDim.x;
+            if (t >= ntiles) break;
+            for (int l = 0; l < nl && ok; l++) {
+                const int nch = p.L[l].nch, Np = p.L[l].Np;
+                if (l == 0) {  // the input layer: chunks 0 and 1 from global memory
+                    stage_halves(p, ag, af, t_base, r, 3, t, 0, 0, j);
+                    if (nch > 1) stage_halves(p, ag, af, t_base, r, 3, t, 0, 1, j + 1);
+                }
+                {  // the accumulators start at the bias (zero beyond Np)
+                    const uint32_t b_addr = smem_u32(sbias + l * 128);
+#pragma unroll
+                    for (int q = 0; q < 32; q++)
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(acc[4 * q]), "=f"(acc[4 * q + 1]), "=f"(acc[4 * q + 2]), "=f"(acc[4 * q + 3])
+                                     : "r"(b_addr + 16u * q));
+                }
+                for (int c = 0; c < nch && ok; c++) {
+                    const uint32_t jj = j + (uint32_t)c;
+                    const int s = jj & 1;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&p_full[g], pu & 1, p.err, 6, (l << 8) | c, (int)pu,
+                                                           (int)jj, slot));
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int q0 = 0; q0 < 8; q0 += 4) {
+                        if (16 * q0 < Np) {
+                            uint32_t v[4][16];
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (16 * (q0 + u) < Np)
+                                    tmem_ld16_nw(lane_base + kPCol + (uint32_t)(128 * g + 16 * (q0 + u)), v[u]);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (16 * (q0 + u) < Np) {
+#pragma unroll
+                                    for (int e = 0; e < 16; e += 2)
+                                        add2(acc[16 * (q0 + u) + e], acc[16 * (q0 + u) + e + 1], v[u][e], v[u][e + 1]);
+                                }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&p_empty[g]);
+                    pu++;
+                    // the hand-over takes the last chunk's a_empty
+                    if (c == nch - 1 && l + 1 < nl) break;
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(&ae[s], (jj >> 1) & 1, p.err, 5, (l << 8) | c, (int)jj, (int)pu, slot));
+                    if (!ok) break;
+                    if (c + 2 < nch) stage_halves(p, ag, af, t_base, r, 3, t, l, c + 2, jj + 2);
+                }
+                j += (uint32_t)nch;
+                if (!ok) break;
+                const bool last = l + 1 == nl;
+                if (last && p.tail_n > 0) {  // the CUDA-core tail over all of this tile's columns
+                    const long long row = (long long)t * kBM + r;
+                    const float *btail = sbias + nl * 128;
+                    if (p.tail_np == 8) {
+                        float o[8];
+                        switch (p.L[l].act) {
+                            case 1: tail_dots<1, 8>(o, acc, stail, 0, Np); break;
+                            case 2: tail_dots<2, 8>(o, acc, stail, 0, Np); break;
+                            case 3: tail_dots<3, 8>(o, acc, stail, 0, Np); break;
+                            default: tail_dots<0, 8>(o, acc, stail, 0, Np); break;
+                        }
+                        write_tail_row<8>(p, o, btail, row);
+                    } else {
+                        float o[16];
+                        switch (p.L[l].act) {
+                            case 1: tail_dots<1, 16>(o, acc, stail, 0, Np); break;
+                            case 2: tail_dots<2, 16>(o, acc, stail, 0, Np); break;
+                            case 3: tail_dots<3, 16>(o, acc, stail, 0, Np); break;
+                            default: tail_dots<0, 16>(o, acc, stail, 0, Np); break;
+                        }
+                        write_tail_row<16>(p, o, btail, row);
+                    }
+                } else if (last) {  // the last layer to global memory
+                    switch (p.L[l].act) {
+                        case 1: finalize_half<1>(p, acc, p.L[l].N, 0, lane_base, true, t, r); break;
+                        case 2: finalize_half<2>(p, acc, p.L[l].N, 0, lane_base, true, t, r); break;
+                        case 3: finalize_half<3>(p, acc, p.L[l].N, 0, lane_base, true, t, r); break;
+                        default: finalize_half<0>(p, acc, p.L[l].N, 0, lane_base, true, t, r); break;
+                    }
+                } else {
+                    // Hand-over: chunk 0 of the next layer straight from the registers into
+                    // the slot of chunk j-2 (seen consumed), columns 64..127 into this group's
+                    // T for the later chunks, chunk 1 once the last chunk's slot is free.
+                    switch (p.L[l].act) {
+                        case 1: act_in_place<1>(acc); break;
+                        case 2: act_in_place<2>(acc); break;
+                        case 3: act_in_place<3>(acc); break;
+                        default: break;
+                    }
+                    stage_from_regs<0>(ag, af, r, acc, j);
+#pragma unroll
+                    for (int q = 4; q < 8; q++) {
+                        float v[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) v[e] = acc[16 * q + e];
+                        tmem_st16(t_base + kTCol + (uint32_t)(16 * q), v);
+                    }
+                    const uint32_t jl = j - 1;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&ae[jl & 1], (jl >> 1) & 1, p.err, 5, (l << 8) | (nch - 1),
+                                                           (int)jl, (int)pu, slot));
+                    if (!ok) break;
+                    if (p.L[l + 1].nch > 1) stage_from_regs<32>(ag, af, r, acc, j + 1);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
                 }
             }
         }
@@ -1146,18 +1470,21 @@ __global__ void __launch_bounds__(kThreadsWs, 1) lstm_tc_kernel(const __grid_con
 size_t mlp_tc_smem_bytes() { return 1024 + kSmemB + kSmemA + kSmemBias + kSmemTailW + kSmemX + kSmemBars; }
 
 bool tc_register_split_ok() {
-    cudaFuncAttributes a{}, b{};
+    cudaFuncAttributes a{}, b{}, c{};
     if (cudaFuncGetAttributes(&a, mlp_tc_kernel) != cudaSuccess ||
-        cudaFuncGetAttributes(&b, lstm_tc_kernel) != cudaSuccess) {
+        cudaFuncGetAttributes(&b, lstm_tc_kernel) != cudaSuccess ||
+        cudaFuncGetAttributes(&c, mlp_tc_dual_kernel) != cudaSuccess) {
         (void)cudaGetLastError();
         return true;
     }
-    return a.numRegs == kLaunchRegs && b.numRegs == kLaunchRegs;
+    return a.numRegs == kLaunchRegs && b.numRegs == kLaunchRegs && c.numRegs == kLaunchRegs;
 }
 
 cudaError_t mlp_tc_configure() {
     cudaError_t e =
         cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_smem_bytes());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(mlp_tc_dual_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mlp_tc_dual_smem());
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(lstm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lstm_tc_smem());
 }
@@ -1177,15 +1504,25 @@ cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st) {
 
 cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st) {
     const long long tiles = (a.n + kBM - 1) / kBM;
-    const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-    if (grid <= 0) return cudaSuccess;
     // setmaxnreg redistributes the registers the block was launched with: the
     // split only fits (and only ever completes) at exactly kLaunchRegs a thread
     static const int regs = [] {
-        cudaFuncAttributes fa{};
-        return cudaFuncGetAttributes(&fa, mlp_tc_kernel) == cudaSuccess ? fa.numRegs : -1;
+        cudaFuncAttributes fa{}, fb{};
+        if (cudaFuncGetAttributes(&fa, mlp_tc_kernel) != cudaSuccess ||
+            cudaFuncGetAttributes(&fb, mlp_tc_dual_kernel) != cudaSuccess)
+            return -1;
+        return fa.numRegs == fb.numRegs ? fa.numRegs : -1;
     }();
     if (regs != kLaunchRegs) return cudaErrorInvalidConfiguration;
+    if (a.dual) {  // two tiles per CTA at a time, one per column group
+        const long long pairs = (tiles + 1) / 2;
+        const int grid = (int)(pairs < num_sms ? pairs : num_sms);
+        if (grid <= 0) return cudaSuccess;
+        mlp_tc_dual_kernel<<<grid, kThreadsWs, mlp_tc_dual_smem(), st>>>(a);
+        return cudaGetLastError();
+    }
+    const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+    if (grid <= 0) return cudaSuccess;
     mlp_tc_kernel<<<grid, kThreadsWs, mlp_tc_smem_bytes(), st>>>(a);
     return cudaGetLastError();
 }

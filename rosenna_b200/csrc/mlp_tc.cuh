@@ -34,6 +34,9 @@ struct TcArgs {
     // FFMA kernel's layout), bias [tail_np] at tail_b_off.
     int tail_n, tail_np, tail_k, tail_kp, tail_act;
     long long tail_w_off, tail_b_off;
+    // every layer's Np <= 128: run mlp_tc_dual_kernel (each column group its
+    // own tile) instead of splitting one tile's columns between the groups
+    int dual;
 };
 
 // One LSTM layer (fLibrary/layers.f90 lstm / lstm_cell) on the tensor cores,

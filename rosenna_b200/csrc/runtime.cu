@@ -535,6 +535,12 @@ Status do_initialize(const std::string &model, const std::string &weights, const
                 if (!mlp_tc_encode_map(&a.maps[l], d->arena + ly.tc_w_off, ly.tc_Kp, ly.tc_Np, &why))
                     return Status::Err(ROSENNA_ERR_CUDA, why);
             }
+            // no layer wider than 128: each column group takes a tile of its own
+            // (ROSENNA_TC_DUAL=0 splits one tile's columns between the groups instead)
+            bool narrow = true;
+            for (int l = 0; l < a.nlayers; l++) narrow = narrow && a.L[l].Np <= 128;
+            const char *dual_env = getenv("ROSENNA_TC_DUAL");
+            a.dual = narrow && !(dual_env && std::string(dual_env) == "0") ? 1 : 0;
         }
         for (auto &s : d->slots) {
             CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));

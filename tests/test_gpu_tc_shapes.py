@@ -1,7 +1,10 @@
-"""Tensor-core MLP kernel on many chain shapes: widths around the 16/32/128
-boundaries of its tiling (N multiple of 16 per half, K chunks of 32, two
-column halves of 128), depths up to its 8-layer limit, every activation, the
-CUDA-core tail on and off, batches that leave partial 128-sample tiles.
+"""Tensor-core MLP kernels on many chain shapes: widths around the 16/32/128
+boundaries of their tiling (N multiple of 16 per half, K chunks of 32, two
+column halves of 128), depths up to the 8-layer limit, every activation, the
+CUDA-core tail on and off, batches that leave partial 128-sample tiles (and,
+for chains no wider than 128, an odd tile left over for one column group).
+Chains no wider than 128 run both on the kernel that gives each column group
+a tile of its own (the default) and on the one that splits a tile's columns.
 Compared with the fp64 oracle at |gpu - ref| <= 1e-5 + 1e-4 |ref|."""
 import os
 
@@ -28,6 +31,8 @@ CASES = {
     "two_cols_in_half_1": ([5, 130, 3], ["relu", "none"]),
     "all_narrow": ([16, 16, 16, 16], ["tanh", "tanh", "none"]),
     "ragged": ([20, 50, 70, 9], ["sigmoid", "relu", "none"]),
+    "narrow_deep": ([40] + [96] * 7 + [12], ["relu"] * 7 + ["none"]),
+    "narrow_long_input": ([300, 96, 64, 3], ["tanh", "sigmoid", "none"]),
 }
 
 
@@ -51,19 +56,25 @@ def _device():
     yield
 
 
+def narrow(case):
+    return max(CASES[case][0][1:]) <= 128
+
+
 @pytest.mark.parametrize("tail", ["1", "0"])
-@pytest.mark.parametrize("case", sorted(CASES))
-def test_tc_chain_shapes(case, tail, tmp_path, monkeypatch):
+@pytest.mark.parametrize("case,dual", [(c, d) for c in sorted(CASES) for d in (("1", "0") if narrow(c) else ("1",))])
+def test_tc_chain_shapes(case, tail, dual, tmp_path, monkeypatch):
     monkeypatch.setenv("ROSENNA_MLP_PATH", "tc")
     monkeypatch.setenv("ROSENNA_TC_TAIL", tail)
+    monkeypatch.setenv("ROSENNA_TC_DUAL", dual)
     d = str(tmp_path)
     widths = build(case, d)
     api.initialize(d)
     assert "mlp_tc" in api.plan_description(), api.plan_description()
     oracle = OracleModel(d)
     rng = np.random.default_rng(len(case) * 7 + int(tail))
-    for n in (1, 129, 1000, 4097):
+    # 50001 samples: 391 tiles, more than one pair of tiles for some CTAs
+    for n in (1, 129, 1000, 4097) + ((50001,) if narrow(case) and dual == "1" else ()):
         x = rng.uniform(-1.5, 1.5, size=(widths[0], n)).astype(np.float32)
         out = api.use_model_rows([x])[0]
         ref = oracle.run_batched(n, [x], [1], [1])[0]
-        assert_close(out, ref.reshape(out.shape), f"{case} tail={tail} n={n}")
+        assert_close(out, ref.reshape(out.shape), f"{case} tail={tail} dual={dual} n={n}")
