@@ -53,10 +53,6 @@ def parse():
     return p.parse_args()
 
 
-def dist_env():
-    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
-
-
 def cpu_baseline(name, model_dir, target_seconds=12.0, steps=1):
     """fp64 oracle, use_model once per sample over all host threads."""
     from oracle import oracle as O
@@ -183,7 +179,9 @@ def measured_fp32_peak(torch):
 
 
 def run_reference(args):
-    rank, _, world = dist_env()
+    from rosenna_b200 import ranks
+
+    rank, _, world = ranks.env()
     if rank != 0:
         return
     from rosenna_b200 import workloads
@@ -212,9 +210,9 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from rosenna_b200 import api, workloads
+    from rosenna_b200 import api, ranks, workloads
 
-    rank, local, world = dist_env()
+    rank, local, world = ranks.env()
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
@@ -236,13 +234,6 @@ def main():
         if world > 1:
             dist.barrier()
 
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     # ---- device-resident throughput ----
     for _ in range(max(3, args.warmup)):
         api.use_model_device(n, in_ptrs, out_ptrs, stream.cuda_stream)
@@ -258,7 +249,7 @@ def main():
             launches += api.last_launch_count()
         e1.record(stream)
         torch.cuda.synchronize()
-    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    t_dev = ranks.max_over_ranks(e0.elapsed_time(e1) / 1e3)
     barrier()
     torch.cuda.synchronize()
     value = world * n * args.steps / t_dev
@@ -274,7 +265,7 @@ def main():
     t0 = time.perf_counter()
     for _ in range(args.steps):
         api.use_model_ptrs(n, hi, ho)
-    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    t_e2e = ranks.max_over_ranks(time.perf_counter() - t0)
     e2e = {"value": world * n * args.steps / t_e2e, "unit": "samples/s",
            "h2d_bytes_per_step": sum(x.numel() * 4 for x in h_in), "d2h_bytes_per_step": sum(o.numel() * 4 for o in h_out),
            "api": "rosenna_use_model_f32 (host arrays, pinned)"}
