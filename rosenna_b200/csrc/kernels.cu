@@ -228,7 +228,11 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
 }
 
 // ---- LSTM ----------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p) {
+// kPerSm CTAs per SM: with 2 (<= 128 registers a thread, for tiles whose
+// shared memory lets two fit) one tile's barrier and gate activations overlap
+// the other tile's FMA loop.
+template <int kPerSm>
+__global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmArgs p) {
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, S = p.S, Ip = p.Ip, Hp = p.Hp, G = 4 * Hp, K = Ip + Hp;
     float *W = sm;                        // [K][G]
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
             act[0][(Ip + j) * S + s] = v;
         }
         cp_async_commit();
-        float c[2][8], h[2][8];
+        float c[2][8];
 #pragma unroll
         for (int u = 0; u < 2; u++)
 #pragma unroll
@@ -279,7 +283,6 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
                     else if (p.c0_const >= 0) v = p.arena[p.c0_const + unit];
                 }
                 c[u][j] = v;
-                h[u][j] = 0.f;
             }
         cp_async_wait_all();
         __syncthreads();
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
                 for (int i = 0; i < 8; i++)
 #pragma unroll
                     for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
-#pragma unroll 4
+#pragma unroll(kPerSm == 1 ? 4 : 2)
                 for (int k = 0; k < K; k++) {
                     const float4 a0 = *reinterpret_cast<const float4 *>(A + k * S + s0);
                     const float4 a1 = *reinterpret_cast<const float4 *>(A + k * S + sh + s0);
@@ -316,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
                 for (int u = 0; u < 2; u++) {
                     const int cb = u ? c1l : c0l, unit = u ? u1 : u0;
                     const float bi = bias[cb], bf = bias[cb + 1], bg = bias[cb + 2], bo = bias[cb + 3];
+                    float h[8];
 #pragma unroll
                     for (int j = 0; j < 8; j++) {
                         const float ig = act_sigmoid(acc[4 * u][j] + bi);
@@ -323,17 +327,17 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
                         const float gg = act_tanh(acc[4 * u + 2][j] + bg);
                         const float og = act_sigmoid(acc[4 * u + 3][j] + bo);
                         c[u][j] = fg * c[u][j] + ig * gg;
-                        h[u][j] = og * act_tanh(c[u][j]);
+                        h[j] = og * act_tanh(c[u][j]);
                     }
                     float *hr = Nx + (size_t)(Ip + unit) * S;
-                    *reinterpret_cast<float4 *>(hr + s0) = make_float4(h[u][0], h[u][1], h[u][2], h[u][3]);
-                    *reinterpret_cast<float4 *>(hr + sh + s0) = make_float4(h[u][4], h[u][5], h[u][6], h[u][7]);
+                    *reinterpret_cast<float4 *>(hr + s0) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4 *>(hr + sh + s0) = make_float4(h[4], h[5], h[6], h[7]);
                     if (p.y && unit < p.H) {
                         float *yr = p.y + (long long)(t + p.T * unit) * p.ld_y + n0;
 #pragma unroll
                         for (int j = 0; j < 8; j++) {
                             const int s = (j < 4 ? s0 + j : sh + s0 + j - 4);
-                            if (s < nval) yr[s] = h[u][j];
+                            if (s < nval) yr[s] = h[j];
                         }
                     }
                 }
@@ -342,6 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
             __syncthreads();
         }
         if (active) {
+            // h_T is the last step's h row block (act[T & 1]; the step's barrier published it)
+            const float *hT = act[p.T & 1];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const int unit = u ? u1 : u0;
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) lstm_ffma_kernel(const LstmArgs p
                 for (int j = 0; j < 8; j++) {
                     const int s = (j < 4 ? s0 + j : sh + s0 + j - 4);
                     if (s >= nval) continue;
-                    if (p.hn) p.hn[(long long)unit * p.ld_hn + n0 + s] = h[u][j];
+                    if (p.hn) p.hn[(long long)unit * p.ld_hn + n0 + s] = hT[(size_t)(Ip + unit) * S + s];
                     if (p.cn) p.cn[(long long)unit * p.ld_cn + n0 + s] = c[u][j];
                 }
             }
@@ -602,7 +608,9 @@ size_t lstm_smem_bytes(int Ip, int Hp, int *S_out) {
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(mlp_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(lstm_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    e = cudaFuncSetAttribute(lstm_ffma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(lstm_ffma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
 }
 
 cudaError_t launch_mlp(MlpArgs a, const MlpLayerDev *L, int num_sms, cudaStream_t st) {
@@ -631,10 +639,17 @@ cudaError_t launch_lstm(LstmArgs a, int num_sms, cudaStream_t st) {
     size_t bytes = lstm_smem_bytes(a.Ip, a.Hp, &S);
     if (!bytes) return cudaErrorInvalidConfiguration;
     a.S = S;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lstm_ffma_kernel<2>, kThreads, bytes) != cudaSuccess)
+        per_sm = 0;
+    const bool two = per_sm >= 2;
     const long long tiles = (a.n + S - 1) / S;
-    const int grid = (int)std::min<long long>(tiles, num_sms);
+    const int grid = (int)std::min<long long>(tiles, (long long)num_sms * (two ? 2 : 1));
     if (grid <= 0) return cudaSuccess;
-    lstm_ffma_kernel<<<grid, kThreads, bytes, st>>>(a);
+    if (two)
+        lstm_ffma_kernel<2><<<grid, kThreads, bytes, st>>>(a);
+    else
+        lstm_ffma_kernel<1><<<grid, kThreads, bytes, st>>>(a);
     return cudaGetLastError();
 }
 
