@@ -102,13 +102,13 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
     __shared__ MlpLayerDev L[kMaxMlpLayers];
     const int tid = threadIdx.x, S = p.S, nl = p.nlayers;
     if (tid < nl) L[tid] = p.layers[tid];
-    float *act[2] = {sm, sm + (size_t)p.hid_rows * S};
-    float *stW[2], *stA[2];
-    stW[0] = act[1] + (size_t)p.hid_rows * S;
-    stW[1] = stW[0] + kKC * p.max_mp;
-    stA[0] = stW[1] + kKC * p.max_mp;
-    stA[1] = stA[0] + (size_t)p.stage_a_rows * S;
-    float *bias = stA[1] + (size_t)p.stage_a_rows * S;
+    // double-buffered regions, addressed as offsets from the shared base (an
+    // array of pointers would live in local memory and make the loads generic)
+    const int act_sz = p.hid_rows * S, stw_sz = kKC * p.max_mp, sta_sz = p.stage_a_rows * S;
+    float *const act0 = sm;                  // two [hid_rows][S] activation blocks
+    float *const stW0 = act0 + 2 * act_sz;   // two [kKC][max_mp] weight chunks
+    float *const stA0 = stW0 + 2 * stw_sz;   // two [stage_a_rows][S] input chunks
+    float *bias = stA0 + 2 * sta_sz;
     __syncthreads();
     {
         int bo = 0;
@@ -126,11 +126,11 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
         const int k0 = c * kKC, kc = min(kKC, L[l].Kp - k0), mp = L[l].Mp;
         const float *src = p.arena + L[l].w_off + (long long)k0 * mp;
         const int nv = kc * mp / 4;
-        for (int i = tid; i < nv; i += kThreads) cp_async16(stW[st] + 4 * i, src + 4 * i);
+        for (int i = tid; i < nv; i += kThreads) cp_async16(stW0 + st * stw_sz + 4 * i, src + 4 * i);
         if (l == 0) {
             long long n0 = t * S;
             int nval = (int)min((long long)S, p.n - n0);
-            stage_rows(stA[st], p.in + n0, p.ld_in, k0, kc, L[0].K, S, nval, in_vec && (n0 & 3) == 0);
+            stage_rows(stA0 + st * sta_sz, p.in + n0, p.ld_in, k0, kc, L[0].K, S, nval, in_vec && (n0 & 3) == 0);
         }
         cp_async_commit();
     };
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
             const bool active = tid < mg_n * sg_n;
             const int mg = tid % mg_n, sg = tid / mg_n;
             const int m0 = mg * 4, s0 = sg * 4, mh = Mp >> 1, sh = S >> 1;
-            const float *aprev = act[(l + 1) & 1];
+            const float *aprev = act0 + ((l + 1) & 1) * act_sz;
             float acc[8][8];
 #pragma unroll
             for (int i = 0; i < 8; i++)
@@ -162,8 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
                 else if (l + 1 < nl) issue(tile, l + 1, 0, st ^ 1);
                 else if (tile + gridDim.x < ntiles) issue(tile + gridDim.x, 0, 0, st ^ 1);
                 if (active) {
-                    const float *W = stW[st];
-                    const float *A = (l == 0) ? stA[st] : aprev + (size_t)c * kKC * S;
+                    const float *W = stW0 + st * stw_sz;
+                    const float *A = (l == 0) ? stA0 + st * sta_sz : aprev + c * kKC * S;
                     const int kc = min(kKC, Kp - c * kKC);
 #pragma unroll 4
                     for (int kk = 0; kk < kc; kk++) {
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
                     for (int j = 0; j < 8; j++) acc[i][j] = apply_act(acc[i][j] + b, actf);
                 }
                 if (l + 1 < nl) {
-                    float *O = act[l & 1];
+                    float *O = act0 + (l & 1) * act_sz;
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int m = (i < 4 ? m0 + i : mh + m0 + i - 4);
@@ -237,7 +237,10 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
     const int tid = threadIdx.x, S = p.S, Ip = p.Ip, Hp = p.Hp, G = 4 * Hp, K = Ip + Hp;
     float *W = sm;                        // [K][G]
     float *bias = W + (size_t)K * G;      // [G]
-    float *act[2] = {bias + G, bias + G + (size_t)K * S};  // [K][S] each: rows 0..Ip-1 = x_t, Ip.. = h
+    // two [K][S] blocks (rows 0..Ip-1 = x_t, Ip.. = h), addressed as offsets from
+    // the shared base so every operand load stays a shared-space load
+    float *const actb = bias + G;
+    const int act_sz = K * S;
     {
         const float4 *src = reinterpret_cast<const float4 *>(p.arena + p.w_off);
         for (int i = tid; i < K * G / 4; i += kThreads) cp_async16(W + 4 * i, src + i);
@@ -256,11 +259,11 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
         const long long n0 = tile * S;
         const int nval = (int)min((long long)S, p.n - n0);
         const bool vec = x_vec && (n0 & 3) == 0;
-        __syncthreads();  // previous tile finished with act[]
-        // x_0 into act[0] rows [0, Ip) (rows >= I zero); zero the padding rows of act[1]
-        stage_rows(act[0], p.x + n0, (long long)p.T * p.ld_x, 0, Ip, p.I, S, nval, vec);
-        for (int i = tid; i < (Ip - p.I) * S; i += kThreads) act[1][p.I * S + i] = 0.f;
-        // h0 into act[0] rows [Ip, Ip+Hp)
+        __syncthreads();  // previous tile finished with the activation blocks
+        // x_0 into block 0 rows [0, Ip) (rows >= I zero); zero the padding rows of block 1
+        stage_rows(actb, p.x + n0, (long long)p.T * p.ld_x, 0, Ip, p.I, S, nval, vec);
+        for (int i = tid; i < (Ip - p.I) * S; i += kThreads) actb[act_sz + p.I * S + i] = 0.f;
+        // h0 into block 0 rows [Ip, Ip+Hp)
         for (int i = tid; i < Hp * S; i += kThreads) {
             int j = i / S, s = i - j * S;
             float v = 0.f;
@@ -268,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
                 if (p.h0) v = p.h0[(long long)j * p.ld_h0 + n0 + s];
                 else if (p.h0_const >= 0) v = p.arena[p.h0_const + j];
             }
-            act[0][(Ip + j) * S + s] = v;
+            actb[(Ip + j) * S + s] = v;
         }
         cp_async_commit();
         float c[2][8];
@@ -287,8 +290,8 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
         cp_async_wait_all();
         __syncthreads();
         for (int t = 0; t < p.T; t++) {
-            const float *A = act[t & 1];
-            float *Nx = act[(t + 1) & 1];
+            const float *A = actb + (t & 1) * act_sz;
+            float *Nx = actb + ((t + 1) & 1) * act_sz;
             if (t + 1 < p.T) {
                 // x_{t+1}: row (t+1) + T*i of the input
                 stage_rows(Nx, p.x + (long long)(t + 1) * p.ld_x + n0, (long long)p.T * p.ld_x, 0, p.I, p.I, S, nval,
@@ -296,11 +299,13 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
                 cp_async_commit();
             }
             if (active) {
-                float acc[8][8];
+                float acc[8][8];  // starts from the gate biases (b_ih + b_hh)
 #pragma unroll
-                for (int i = 0; i < 8; i++)
+                for (int i = 0; i < 8; i++) {
+                    const float bv = bias[i < 4 ? c0l + i : c1l + i - 4];
 #pragma unroll
-                    for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+                    for (int j = 0; j < 8; j++) acc[i][j] = bv;
+                }
 #pragma unroll(kPerSm == 1 ? 4 : 2)
                 for (int k = 0; k < K; k++) {
                     const float4 a0 = *reinterpret_cast<const float4 *>(A + k * S + s0);
@@ -317,15 +322,14 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
                 // gates of unit u are acc rows 4u..4u+3 (i, f, g, o), layers.f90:88-96
 #pragma unroll
                 for (int u = 0; u < 2; u++) {
-                    const int cb = u ? c1l : c0l, unit = u ? u1 : u0;
-                    const float bi = bias[cb], bf = bias[cb + 1], bg = bias[cb + 2], bo = bias[cb + 3];
+                    const int unit = u ? u1 : u0;
                     float h[8];
 #pragma unroll
                     for (int j = 0; j < 8; j++) {
-                        const float ig = act_sigmoid(acc[4 * u][j] + bi);
-                        const float fg = act_sigmoid(acc[4 * u + 1][j] + bf);
-                        const float gg = act_tanh(acc[4 * u + 2][j] + bg);
-                        const float og = act_sigmoid(acc[4 * u + 3][j] + bo);
+                        const float ig = act_sigmoid(acc[4 * u][j]);
+                        const float fg = act_sigmoid(acc[4 * u + 1][j]);
+                        const float gg = act_tanh(acc[4 * u + 2][j]);
+                        const float og = act_sigmoid(acc[4 * u + 3][j]);
                         c[u][j] = fg * c[u][j] + ig * gg;
                         h[j] = og * act_tanh(c[u][j]);
                     }
@@ -346,8 +350,8 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
             __syncthreads();
         }
         if (active) {
-            // h_T is the last step's h row block (act[T & 1]; the step's barrier published it)
-            const float *hT = act[p.T & 1];
+            // h_T is the h rows of block T & 1 (the last step's barrier published them)
+            const float *hT = actb + (p.T & 1) * act_sz;
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const int unit = u ? u1 : u0;
