@@ -231,10 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_ffma_kernel(const MlpArgs p) 
 // kPerSm CTAs per SM: with 2 (<= 128 registers a thread, for tiles whose
 // shared memory lets two fit) one tile's barrier and gate activations overlap
 // the other tile's FMA loop.
-template <int kPerSm>
+// kHp > 0: the padded hidden size and the tile (S = 8 * kThreads / (kHp / 2)
+// samples) are compile-time constants, so every operand load is a base register
+// plus an immediate offset; kHp = 0 reads both from the arguments.
+template <int kHp>
+constexpr int lstm_tile_samples() { return kHp ? (8 * kThreads / (kHp / 2) < 256 ? 8 * kThreads / (kHp / 2) : 256) : 0; }
+template <int kPerSm, int kHp>
 __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmArgs p) {
     extern __shared__ __align__(16) float sm[];
-    const int tid = threadIdx.x, S = p.S, Ip = p.Ip, Hp = p.Hp, G = 4 * Hp, K = Ip + Hp;
+    const int tid = threadIdx.x, S = kHp ? lstm_tile_samples<kHp>() : p.S, Ip = p.Ip, Hp = kHp ? kHp : p.Hp,
+              G = 4 * Hp, K = Ip + Hp;
     float *W = sm;                        // [K][G]
     float *bias = W + (size_t)K * G;      // [G]
     // two [K][S] blocks (rows 0..Ip-1 = x_t, Ip.. = h), addressed as offsets from
@@ -612,9 +618,11 @@ size_t lstm_smem_bytes(int Ip, int Hp, int *S_out) {
 cudaError_t configure_kernels() {
     cudaError_t e = cudaFuncSetAttribute(mlp_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(lstm_ffma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    e = cudaFuncSetAttribute(lstm_ffma_kernel<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(lstm_ffma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    e = cudaFuncSetAttribute(lstm_ffma_kernel<2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(lstm_ffma_kernel<2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
 }
 
 cudaError_t launch_mlp(MlpArgs a, const MlpLayerDev *L, int num_sms, cudaStream_t st) {
@@ -644,16 +652,18 @@ cudaError_t launch_lstm(LstmArgs a, int num_sms, cudaStream_t st) {
     if (!bytes) return cudaErrorInvalidConfiguration;
     a.S = S;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lstm_ffma_kernel<2>, kThreads, bytes) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lstm_ffma_kernel<2, 0>, kThreads, bytes) != cudaSuccess)
         per_sm = 0;
     const bool two = per_sm >= 2;
     const long long tiles = (a.n + S - 1) / S;
     const int grid = (int)std::min<long long>(tiles, (long long)num_sms * (two ? 2 : 1));
     if (grid <= 0) return cudaSuccess;
-    if (two)
-        lstm_ffma_kernel<2><<<grid, kThreads, bytes, st>>>(a);
+    if (two && a.Hp == 32 && S == lstm_tile_samples<32>())
+        lstm_ffma_kernel<2, 32><<<grid, kThreads, bytes, st>>>(a);
+    else if (two)
+        lstm_ffma_kernel<2, 0><<<grid, kThreads, bytes, st>>>(a);
     else
-        lstm_ffma_kernel<1><<<grid, kThreads, bytes, st>>>(a);
+        lstm_ffma_kernel<1, 0><<<grid, kThreads, bytes, st>>>(a);
     return cudaGetLastError();
 }
 
