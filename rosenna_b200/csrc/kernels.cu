@@ -305,15 +305,24 @@ __global__ void __launch_bounds__(kThreads, kPerSm) lstm_ffma_kernel(const LstmA
                 cp_async_commit();
             }
             if (active) {
-                float acc[8][8];  // starts from the gate biases (b_ih + b_hh)
+                float acc[8][8];
+                {  // k = 0 accumulates onto the gate biases (b_ih + b_hh)
+                    const float4 b0 = *reinterpret_cast<const float4 *>(bias + c0l);
+                    const float4 b1 = *reinterpret_cast<const float4 *>(bias + c1l);
+                    const float4 a0 = *reinterpret_cast<const float4 *>(A + s0);
+                    const float4 a1 = *reinterpret_cast<const float4 *>(A + sh + s0);
+                    const float4 w0 = *reinterpret_cast<const float4 *>(W + c0l);
+                    const float4 w1 = *reinterpret_cast<const float4 *>(W + c1l);
+                    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                    const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float bv = bias[i < 4 ? c0l + i : c1l + i - 4];
+                    for (int i = 0; i < 8; i++)
 #pragma unroll
-                    for (int j = 0; j < 8; j++) acc[i][j] = bv;
+                        for (int j = 0; j < 8; j++) acc[i][j] = fmaf(w[i], a[j], bv[i]);
                 }
 #pragma unroll(kPerSm == 1 ? 4 : 2)
-                for (int k = 0; k < K; k++) {
+                for (int k = 1; k < K; k++) {
                     const float4 a0 = *reinterpret_cast<const float4 *>(A + k * S + s0);
                     const float4 a1 = *reinterpret_cast<const float4 *>(A + k * S + sh + s0);
                     const float4 w0 = *reinterpret_cast<const float4 *>(W + k * G + c0l);
