@@ -87,6 +87,18 @@ int rosenna_use_model_f32(int64_t n, const float *const *inputs, float *const *o
 /* The same for fp64 host arrays (converted to fp32 on the host). */
 int rosenna_use_model_f64(int64_t n, const double *const *inputs, double *const *outputs);
 
+#ifndef ROSENNA_NO_LEGACY_USE_MODEL
+/* Replaces modelCreator.fpp:42 use_model(i0,..,o0,..) for fixed-shape callers,
+ * which declare it with their model's own argument count (examples/cAPI.c:3:
+ * void use_model(double *i0, double *o0)): fp64 arrays of the export shapes,
+ * the model's inputs then its outputs, evaluated at the export batch.  Declared
+ * here with the largest count the engine accepts (16 arrays); only the model's
+ * count is read.  A file that declares its own prototype defines
+ * ROSENNA_NO_LEGACY_USE_MODEL before including this header.  The status is kept
+ * for rosenna_last_status()/rosenna_last_error(); the reference aborts instead. */
+void use_model(double *a0, double *a1, double *a2, double *a3, double *a4, double *a5, double *a6, double *a7, double *a8, double *a9, double *a10, double *a11, double *a12, double *a13, double *a14, double *a15);
+#endif
+
 /* Batched use_model on device arrays, on `stream` (a cudaStream_t; NULL = the
  * default stream).  The arrays live on the selected GPU when one is selected,
  * else on the current device.

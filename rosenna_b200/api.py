@@ -28,7 +28,7 @@ EXPORTS = [
     "rosenna_set_devices", "rosenna_last_status", "rosenna_last_error", "rosenna_num_inputs", "rosenna_num_outputs",
     "rosenna_input_shape", "rosenna_output_shape", "rosenna_use_model_f32", "rosenna_use_model_f64",
     "rosenna_use_model_device_f32", "rosenna_use_model_device_noalloc_f32", "rosenna_last_launch_count",
-    "rosenna_plan_description",
+    "rosenna_plan_description", "use_model",
 ]
 
 
@@ -57,6 +57,7 @@ def lib():
     c_int, c_i64, c_char_p, c_void_p = ctypes.c_int, ctypes.c_int64, ctypes.c_char_p, ctypes.c_void_p
     PP = ctypes.POINTER(c_void_p)
     L.initialize.restype = None
+    L.use_model.restype = None
     L.rosenna_initialize.restype = c_int
     L.rosenna_initialize_from.argtypes = [c_char_p, c_char_p, c_char_p]
     L.rosenna_check_model.argtypes = [c_char_p, c_char_p, c_char_p]

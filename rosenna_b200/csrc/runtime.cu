@@ -31,6 +31,7 @@ namespace rosenna {
 namespace {
 
 constexpr int kSlots = 3;  // chunk streams: one's H2D, another's kernels, a third's D2H
+constexpr int kLegacyArgs = 16;  // arrays the fixed-shape use_model symbol takes
 
 struct Slot {
     cudaStream_t stream = nullptr;
@@ -600,6 +601,30 @@ int rosenna_check_model(const char *model_txt, const char *weights_txt, const ch
 int rosenna_initialize(void) { return rosenna_initialize_from("onnxModel.txt", "onnxWeights.txt", "variables.fpp"); }
 
 void initialize(void) { (void)rosenna_initialize(); }
+
+// roseNNa's fixed-shape entry point, SUBROUTINE use_model(i0,..,o0,..)
+// bind(c,name="use_model") (fLibrary/modelCreator.fpp:42), which C code calls as
+// void use_model(double *i0, .., double *o0) (examples/cAPI.c:3): fp64 arrays of
+// the export shapes, the model's inputs then its outputs, evaluated at the
+// export batch.  It takes the largest argument count the engine accepts and
+// reads only the model's own count, so a caller that declares it with that
+// count passes exactly the arguments read.  The status is kept for
+// rosenna_last_status() / rosenna_last_error(); the reference aborts instead.
+void use_model(double *a0, double *a1, double *a2, double *a3, double *a4, double *a5, double *a6, double *a7, double *a8, double *a9, double *a10, double *a11, double *a12, double *a13, double *a14, double *a15) {
+    double *const a[kLegacyArgs] = {a0, a1, a2, a3, a4, a5, a6, a7, a8, a9, a10, a11, a12, a13, a14, a15};
+    if (!g_ctx.ready) {
+        fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+        return;
+    }
+    const Plan &P = g_ctx.plan;
+    if (P.inputs.empty() || P.inputs.size() + P.outputs.size() > (size_t)kLegacyArgs) {
+        fail(ROSENNA_ERR_UNSUPPORTED, "use_model takes at most " + std::to_string(kLegacyArgs) +
+                                          " arrays; call rosenna_use_model_f64 with array lists instead");
+        return;
+    }
+    const IoDesc &d0 = P.inputs[0];
+    (void)rosenna_use_model_f64(d0.shape[(size_t)d0.bdim], a, a + P.inputs.size());
+}
 
 int rosenna_finalize(void) {
     std::lock_guard<std::mutex> lk(g_mu);

@@ -56,6 +56,34 @@ def test_initialize_statuses(tmp_path):
     assert e.value.code == api.ERR_STATE
 
 
+def test_fixed_shape_use_model_before_initialize_is_a_state_error():
+    import ctypes
+
+    api.finalize()
+    L = api.lib()
+    L.use_model(ctypes.c_void_p(0), ctypes.c_void_p(0))  # roseNNa's own two-array call form
+    assert L.rosenna_last_status() == api.ERR_STATE
+
+
+@pytest.mark.parametrize("own_prototype", [True, False])
+def test_header_serves_fixed_shape_callers(own_prototype, tmp_path):
+    """A C file may declare use_model with its model's own argument count (as
+    the reference's examples do) or take the header's declaration."""
+    if not shutil.which("gcc"):
+        pytest.skip("no C compiler")
+    src = tmp_path / "caller.c"
+    proto = "#define ROSENNA_NO_LEGACY_USE_MODEL\n" if own_prototype else ""
+    decl = "void use_model(double *i0, double *o0);\n" if own_prototype else ""
+    call = "use_model(x, y);" if own_prototype else "use_model(x, y, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0);"
+    src.write_text(proto + '#include "rosenna.h"\n' + decl +
+                   "void run(double *x, double *y) { initialize(); " + call + " }\n")
+    import subprocess
+
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
+                        str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
 def test_initialize_without_gpu_reports_no_device():
     import torch
 

@@ -46,6 +46,23 @@ def test_golden_case_at_export_batch(case):
     assert_close(out, goldens.golden(case), case)
 
 
+@pytest.mark.parametrize("case", goldens.cases())
+def test_golden_case_through_fixed_shape_use_model(case):
+    """roseNNa's own entry point, use_model(i0,..,o0,..) on fp64 arrays of the
+    export shapes (the C symbol a fixed-shape caller links against)."""
+    import ctypes
+
+    api.initialize(goldens.case_dir(case))
+    ins = [np.asfortranarray(np.asarray(x, dtype=np.float64).reshape(s, order="A"))
+           for x, (s, _) in zip(goldens.inputs(case), api.input_specs())]
+    outs = [np.zeros(s, dtype=np.float64, order="F") for s, _ in api.output_specs()]
+    L = api.lib()
+    L.use_model(*[ctypes.c_void_p(a.ctypes.data) for a in ins + outs])
+    assert L.rosenna_last_status() == 0, api.lib().rosenna_last_error()
+    assert api.last_launch_count() > 0
+    assert_close(outs[0], goldens.golden(case), case)
+
+
 BATCHED_CASES = [c for c in goldens.cases() if c not in ("conv_basic", "lstm_gemm")]
 
 
