@@ -114,12 +114,30 @@ int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *c
  * from one fixed 64 MiB array in device memory that every GPU loading this
  * library holds until exit; n is rejected (ROSENNA_ERR_SHAPE, with the limit in
  * rosenna_last_error()) when the intermediates for n samples do not fit.  The
- * first call on a device looks up that array's address (set-up); make that
- * first call before any stream capture.  All calls share the array and it keeps
+ * array's address is looked up in initialize(), once per selected GPU with that
+ * GPU current (set-up); with lazy module loading that is also when the array is
+ * created, so the calls themselves allocate nothing.  All calls share the array and it keeps
  * the last call's contents (no intermediate needs clearing: each is written
  * before it is read), so calls whose work overlaps on the GPU race: order them
  * on one stream.  Arguments and layout as for rosenna_use_model_device_f32. */
 int rosenna_use_model_device_noalloc_f32(int64_t n, const float *const *inputs, float *const *outputs, void *stream);
+
+/* Per-step device timing, for benchmarks (no counterpart in roseNNa, whose
+ * generated use_model takes CPU_TIME around its body and discards it,
+ * fLibrary/modelCreator.fpp:77,168).  After rosenna_step_timing_begin(m), the
+ * next use_model calls record a CUDA event pair around every plan step on the
+ * stream the step runs on, for up to m steps in total (per GPU).
+ * rosenna_step_timing_end waits for those events, writes the summed
+ * milliseconds of plan step i to ms[i] and the number of times it ran to
+ * runs[i] (i < max_steps), and stops recording. */
+int rosenna_step_timing_begin(int64_t max_records);
+int rosenna_step_timing_end(double *ms, int64_t *runs, int max_steps);
+
+/* Number of steps of the launch plan, and for step i the kernel that runs it
+ * and its algorithmic flops per sample (2 x the multiply-adds of its Gemm, LSTM
+ * gate and convolution contractions; 0 for data-movement steps). */
+int rosenna_step_count(void);
+int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sample);
 
 /* Number of kernel launches the last use_model call issued (all devices). */
 int64_t rosenna_last_launch_count(void);

@@ -89,11 +89,14 @@ class OracleModel:
             raise RuntimeError("oracle run failed: " + err.value.decode())
         return outs
 
-    def run_batched(self, n, inputs, in_pre, out_pre, threads=0):
-        """Per-sample loop over a batch of n (model exported at batch 1).
+    def run_batched(self, n, inputs, in_pre, out_pre, threads=None):
+        """Per-sample loop over a batch of n (model exported at batch 1), on
+        `threads` OpenMP threads (default: every host core this process may use).
 
         `inputs` are flat float64 arrays in the batched reference layout; returns
         flat float64 outputs in the same layout."""
+        if threads is None:
+            threads = host_cores()
         ins = [np.ascontiguousarray(x, dtype=np.float64).reshape(-1) for x in inputs]
         outs = [np.zeros(int(np.prod(s)) * n, dtype=np.float64) for s in self.output_shapes]
         ip = (ctypes.c_int * len(in_pre))(*in_pre)
@@ -106,4 +109,16 @@ class OracleModel:
 
 
 def max_threads():
+    """OpenMP's default team size (honours OMP_NUM_THREADS)."""
     return _load().ro_max_threads()
+
+
+def host_cores():
+    """Host CPUs this process may run on, whatever OMP_NUM_THREADS says (torchrun
+    sets it to 1); passed explicitly as the oracle's thread count."""
+    import os
+
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1

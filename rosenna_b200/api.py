@@ -28,7 +28,8 @@ EXPORTS = [
     "rosenna_set_devices", "rosenna_last_status", "rosenna_last_error", "rosenna_num_inputs", "rosenna_num_outputs",
     "rosenna_input_shape", "rosenna_output_shape", "rosenna_use_model_f32", "rosenna_use_model_f64",
     "rosenna_use_model_device_f32", "rosenna_use_model_device_noalloc_f32", "rosenna_last_launch_count",
-    "rosenna_plan_description", "use_model",
+    "rosenna_plan_description", "use_model", "rosenna_step_timing_begin", "rosenna_step_timing_end",
+    "rosenna_step_count", "rosenna_step_info",
 ]
 
 
@@ -71,6 +72,9 @@ def lib():
     L.rosenna_use_model_device_noalloc_f32.argtypes = [c_i64, PP, PP, c_void_p]
     L.rosenna_last_launch_count.restype = c_i64
     L.rosenna_plan_description.restype = c_char_p
+    L.rosenna_step_timing_begin.argtypes = [c_i64]
+    L.rosenna_step_timing_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i64), c_int]
+    L.rosenna_step_info.argtypes = [c_int, c_char_p, c_int, ctypes.POINTER(ctypes.c_double)]
     _lib = L
     return L
 
@@ -206,3 +210,34 @@ def use_model_device_noalloc(n: int, in_ptrs: Sequence[int], out_ptrs: Sequence[
     """The allocation-free device entry point (no cudaMalloc/cudaFree during the
     call; intermediates come from a fixed 64 MiB array per GPU, so n is bounded)."""
     _check(lib().rosenna_use_model_device_noalloc_f32(n, _ptrs(in_ptrs), _ptrs(out_ptrs), ctypes.c_void_p(stream)))
+
+
+def step_info():
+    """[(kernel name, algorithmic flops per sample)] per plan step."""
+    n = lib().rosenna_step_count()
+    if n < 0:
+        _check(-n)
+    out = []
+    buf = ctypes.create_string_buffer(128)
+    f = ctypes.c_double()
+    for i in range(n):
+        _check(lib().rosenna_step_info(i, buf, 128, ctypes.byref(f)))
+        out.append((buf.value.decode(), float(f.value)))
+    return out
+
+
+def step_timing_begin(max_records: int) -> None:
+    """Record a CUDA event pair around every plan step of the next calls (up to
+    max_records steps per GPU)."""
+    _check(lib().rosenna_step_timing_begin(max_records))
+
+
+def step_timing_end():
+    """[(summed ms, runs)] per plan step since step_timing_begin."""
+    n = lib().rosenna_step_count()
+    if n < 0:
+        _check(-n)
+    ms = (ctypes.c_double * max(1, n))()
+    runs = (ctypes.c_int64 * max(1, n))()
+    _check(lib().rosenna_step_timing_end(ms, runs, n))
+    return [(float(ms[i]), int(runs[i])) for i in range(n)]

@@ -686,14 +686,13 @@ static cudaError_t launch_conv_tile(const ConvArgs &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
-    const long long outs = (long long)a.OC * a.Hq * a.Wq;
-    if (a.n <= 0 || outs <= 0) return cudaSuccess;
-    // the tiled kernel: stride-1 3x3 convolution with no pool or a pool window
-    // of 2 or 3, 5x5 with no pool or a window of 2 (5x5 under a 3-wide window
-    // spills even at 255 registers); weights and bias within the default 48 KB
-    // of dynamic shared memory.  ROSENNA_CONV_PATH=direct keeps every
-    // convolution on the per-element kernel
+// Which conv kernel runs a step: the tiled kernel (stride-1 3x3 convolution
+// with no pool or a pool window of 2 or 3, 5x5 with no pool or a window of 2;
+// 5x5 under a 3-wide window spills even at 255 registers; weights and bias
+// within the default 48 KB of dynamic shared memory), else the per-element one.
+// ROSENNA_CONV_PATH=direct keeps every convolution on the per-element kernel.
+// Returns KS*10 + pool window for the tiled kernel, 0 for the per-element one.
+static int conv_tile_variant(const ConvArgs &a) {
     static const bool direct_only = [] {
         const char *e = getenv("ROSENNA_CONV_PATH");
         return e && std::string(e) == "direct";
@@ -701,15 +700,33 @@ cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
     const int pk = a.pool == 0 ? 1 : a.pk;
     const int ocb = pk == 3 ? 4 : 8;  // 3x3 pooled windows of 8 channels would not fit 128 registers
     if (!direct_only && a.conv && (a.KS == 3 || a.KS == 5) && a.str_h == 1 && a.str_w == 1 && pk <= (a.KS == 3 ? 3 : 2) &&
-        ((size_t)a.C * a.KS * a.KS + 1) * ((a.OC + ocb - 1) / ocb * ocb) * sizeof(float) <= 48 * 1024) {
-        // 8 output channels per item: two CTAs per SM fit (16 per item spills or halves occupancy)
-        if (a.KS == 3) {
-            if (pk == 1) return launch_conv_tile<3, 1, 8>(a, st);
-            if (pk == 2) return launch_conv_tile<3, 2, 8>(a, st);
-            return launch_conv_tile<3, 3, 4>(a, st);
-        }
-        if (pk == 1) return launch_conv_tile<5, 1, 8>(a, st);
-        return launch_conv_tile<5, 2, 8>(a, st);
+        ((size_t)a.C * a.KS * a.KS + 1) * ((a.OC + ocb - 1) / ocb * ocb) * sizeof(float) <= 48 * 1024)
+        return a.KS * 10 + pk;
+    return 0;
+}
+
+const char *conv_kernel_name(const ConvArgs &a) {
+    switch (conv_tile_variant(a)) {
+        case 31: return "conv_pool_tile_kernel<3,1,8>";
+        case 32: return "conv_pool_tile_kernel<3,2,8>";
+        case 33: return "conv_pool_tile_kernel<3,3,4>";
+        case 51: return "conv_pool_tile_kernel<5,1,8>";
+        case 52: return "conv_pool_tile_kernel<5,2,8>";
+        default: return "conv_pool_kernel";
+    }
+}
+
+cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
+    const long long outs = (long long)a.OC * a.Hq * a.Wq;
+    if (a.n <= 0 || outs <= 0) return cudaSuccess;
+    // 8 output channels per item: two CTAs per SM fit (16 per item spills or halves occupancy)
+    switch (conv_tile_variant(a)) {
+        case 31: return launch_conv_tile<3, 1, 8>(a, st);
+        case 32: return launch_conv_tile<3, 2, 8>(a, st);
+        case 33: return launch_conv_tile<3, 3, 4>(a, st);
+        case 51: return launch_conv_tile<5, 1, 8>(a, st);
+        case 52: return launch_conv_tile<5, 2, 8>(a, st);
+        default: break;
     }
     if (outs > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((a.n + 127) / 128), (unsigned)outs);

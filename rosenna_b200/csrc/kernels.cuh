@@ -64,6 +64,8 @@ struct ConvArgs {
 cudaError_t launch_mlp(MlpArgs a, const MlpLayerDev *host_layers, int num_sms, cudaStream_t st);
 cudaError_t launch_lstm(LstmArgs a, int num_sms, cudaStream_t st);
 cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st);
+// Name of the kernel launch_conv runs for these arguments.
+const char *conv_kernel_name(const ConvArgs &a);
 cudaError_t launch_gather(const float *in, long long ld_in, float *out, long long ld_out, const int *map, long long rows,
                           long long n, cudaStream_t st);
 // add: per-row constant added before the activation, or nullptr

@@ -51,6 +51,15 @@ struct Device {
     std::vector<TcArgs> tc_args;  // per plan step (tensor-core MLP steps only)
     std::vector<TcLstmArgs> lstm_args;  // per plan step (tensor-core LSTM steps only)
     Slot slots[kSlots];
+    // allocation-free entry point: device address of the fixed scratch array,
+    // looked up at initialize (or why it could not be)
+    void *noalloc_base = nullptr;
+    std::string noalloc_err;
+    // per-step timing (rosenna_step_timing_begin/end): event pairs, the plan
+    // step each recorded pair belongs to, pairs used so far
+    std::vector<cudaEvent_t> tev;
+    std::vector<int> tev_step;
+    int64_t tev_used = 0;
 };
 
 struct Context {
@@ -109,6 +118,11 @@ void release_device(Device &d) {
         s.stream = nullptr;
         s.done = nullptr;
     }
+    for (auto e : d.tev) cudaEventDestroy(e);
+    d.tev.clear();
+    d.tev_step.clear();
+    d.tev_used = 0;
+    d.noalloc_base = nullptr;
     cudaFree(d.arena);
     cudaFree(d.err);
     if (d.err_host) cudaFreeHost(d.err_host);
@@ -178,6 +192,9 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
     for (size_t si = 0; si < P.steps.size(); si++) {
         const Step &s = P.steps[si];
         cudaError_t e = cudaSuccess;
+        const bool timed = d.tev_used < (int64_t)d.tev_step.size();
+        if (timed && cudaEventRecord(d.tev[(size_t)(2 * d.tev_used)], stream) != cudaSuccess)
+            return Status::Err(ROSENNA_ERR_CUDA, "cudaEventRecord (step timing) failed");
         switch (s.kind) {
             case Step::MLP: {
                 if (s.tc) {
@@ -295,6 +312,11 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
         }
         if (e != cudaSuccess)
             return Status::Err(ROSENNA_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(e));
+        if (timed) {
+            if (cudaEventRecord(d.tev[(size_t)(2 * d.tev_used + 1)], stream) != cudaSuccess)
+                return Status::Err(ROSENNA_ERR_CUDA, "cudaEventRecord (step timing) failed");
+            d.tev_step[(size_t)d.tev_used++] = (int)si;
+        }
     }
     g_launches += launches;
     return Status::Ok();
@@ -395,6 +417,38 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
     CUDA_TRY(cudaGetLastError());
     if (d.err_host && *(volatile int *)d.err_host) return Status::Err(ROSENNA_ERR_CUDA, tc_error_text(d.err_host));
     return Status::Ok();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free use_model on device arrays (rosenna_use_model_device_noalloc_f32).
+//
+// Some callers cannot have the library allocate device memory while they run:
+// a solver that hands all free GPU memory to its own pool allocator at start-up
+// (cudaMalloc would then fail), or a time-step loop that must not stall, since
+// cudaMalloc/cudaFree synchronise the device.  rosenna_use_model_device_f32
+// allocates its intermediate buffers on first use; that entry point instead
+// carves them from one fixed array in device memory that every GPU loading
+// this library holds until the process exits.  Its address is looked up in
+// initialize(), once per selected device with that device current: with lazy
+// module loading (the CUDA default) that lookup is what loads this file's
+// device module and so creates the array, which therefore happens at
+// initialize, not inside the first allocation-free call.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = (size_t)64 << 20;  // 64 MiB per GPU
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+void noalloc_setup(Device &d) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+        d.noalloc_base = nullptr;
+        d.noalloc_err = std::string("cudaGetSymbolAddress(scratch) at initialize: ") + cudaGetErrorString(e);
+        cudaGetLastError();
+        return;
+    }
+    d.noalloc_base = p;
+    d.noalloc_err.clear();
 }
 
 Status do_initialize(const std::string &model, const std::string &weights, const std::string &vars) {
@@ -547,6 +601,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
             CUDA_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
         }
+        noalloc_setup(*d);
         g_ctx.devs.push_back(std::move(d));
     }
     cudaSetDevice(cur);
@@ -555,6 +610,64 @@ Status do_initialize(const std::string &model, const std::string &weights, const
 }
 
 int report(const Status &st) { return st.ok() ? ok() : fail(st.code, st.msg); }
+
+// Host-array use_model; the caller holds g_mu.
+int use_model_f32_locked(int64_t n, const float *const *inputs, float *const *outputs) {
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    Status st = check_batch(n);
+    if (!st.ok()) return report(st);
+    if (!inputs || !outputs) return fail(ROSENNA_ERR_ARG, "null input/output array list");
+    for (size_t i = 0; i < g_ctx.plan.inputs.size(); i++)
+        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
+    for (size_t i = 0; i < g_ctx.plan.outputs.size(); i++)
+        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
+    g_launches = 0;
+    if (n == 0) return ok();
+    int cur = 0;
+    cudaGetDevice(&cur);
+    const int G = (int)g_ctx.devs.size();
+    std::vector<Status> res((size_t)G);
+    std::vector<std::thread> th;
+    for (int g = 0; g < G; g++) {
+        // contiguous split; the first n % G ranks take one extra sample
+        const int64_t base = n / G, rem = n % G;
+        const int64_t a = g * base + std::min<int64_t>(g, rem), b = a + base + (g < rem ? 1 : 0);
+        th.emplace_back([&, g, a, b] { res[(size_t)g] = host_range(*g_ctx.devs[(size_t)g], n, a, b, inputs, outputs); });
+    }
+    for (auto &t : th) t.join();
+    cudaSetDevice(cur);
+    for (auto &r : res)
+        if (!r.ok()) return report(r);
+    return ok();
+}
+
+// fp64 host arrays converted to fp32 around use_model_f32_locked; the caller
+// holds g_mu, so the plan cannot change (finalize/initialize) during the call.
+int use_model_f64_locked(int64_t n, const double *const *inputs, double *const *outputs) {
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    if (n < 0 || !inputs || !outputs) return fail(ROSENNA_ERR_ARG, "bad arguments");
+    const Plan &P = g_ctx.plan;
+    std::vector<std::vector<float>> fi(P.inputs.size()), fo(P.outputs.size());
+    std::vector<const float *> pi;
+    std::vector<float *> po;
+    for (size_t i = 0; i < P.inputs.size(); i++) {
+        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
+        size_t cnt = (size_t)(P.inputs[i].rows * n);
+        fi[i].resize(cnt);
+        for (size_t k = 0; k < cnt; k++) fi[i][k] = (float)inputs[i][k];
+        pi.push_back(fi[i].data());
+    }
+    for (size_t i = 0; i < P.outputs.size(); i++) {
+        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
+        fo[i].resize((size_t)(P.outputs[i].rows * n));
+        po.push_back(fo[i].data());
+    }
+    int rc = use_model_f32_locked(n, pi.data(), po.data());
+    if (rc) return rc;
+    for (size_t i = 0; i < P.outputs.size(); i++)
+        for (size_t k = 0; k < fo[i].size(); k++) outputs[i][k] = fo[i][k];
+    return ok();
+}
 
 }  // namespace
 }  // namespace rosenna
@@ -612,6 +725,7 @@ void initialize(void) { (void)rosenna_initialize(); }
 // rosenna_last_status() / rosenna_last_error(); the reference aborts instead.
 void use_model(double *a0, double *a1, double *a2, double *a3, double *a4, double *a5, double *a6, double *a7, double *a8, double *a9, double *a10, double *a11, double *a12, double *a13, double *a14, double *a15) {
     double *const a[kLegacyArgs] = {a0, a1, a2, a3, a4, a5, a6, a7, a8, a9, a10, a11, a12, a13, a14, a15};
+    std::lock_guard<std::mutex> lk(g_mu);
     if (!g_ctx.ready) {
         fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
         return;
@@ -623,7 +737,7 @@ void use_model(double *a0, double *a1, double *a2, double *a3, double *a4, doubl
         return;
     }
     const IoDesc &d0 = P.inputs[0];
-    (void)rosenna_use_model_f64(d0.shape[(size_t)d0.bdim], a, a + P.inputs.size());
+    (void)use_model_f64_locked(d0.shape[(size_t)d0.bdim], a, a + P.inputs.size());
 }
 
 int rosenna_finalize(void) {
@@ -661,58 +775,12 @@ int rosenna_output_shape(int i, int64_t *dims, int max_dims, int *bdim) { return
 
 int rosenna_use_model_f32(int64_t n, const float *const *inputs, float *const *outputs) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
-    Status st = check_batch(n);
-    if (!st.ok()) return report(st);
-    if (!inputs || !outputs) return fail(ROSENNA_ERR_ARG, "null input/output array list");
-    for (size_t i = 0; i < g_ctx.plan.inputs.size(); i++)
-        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
-    for (size_t i = 0; i < g_ctx.plan.outputs.size(); i++)
-        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
-    g_launches = 0;
-    if (n == 0) return ok();
-    int cur = 0;
-    cudaGetDevice(&cur);
-    const int G = (int)g_ctx.devs.size();
-    std::vector<Status> res((size_t)G);
-    std::vector<std::thread> th;
-    for (int g = 0; g < G; g++) {
-        // contiguous split; the first n % G ranks take one extra sample
-        const int64_t base = n / G, rem = n % G;
-        const int64_t a = g * base + std::min<int64_t>(g, rem), b = a + base + (g < rem ? 1 : 0);
-        th.emplace_back([&, g, a, b] { res[(size_t)g] = host_range(*g_ctx.devs[(size_t)g], n, a, b, inputs, outputs); });
-    }
-    for (auto &t : th) t.join();
-    cudaSetDevice(cur);
-    for (auto &r : res)
-        if (!r.ok()) return report(r);
-    return ok();
+    return use_model_f32_locked(n, inputs, outputs);
 }
 
 int rosenna_use_model_f64(int64_t n, const double *const *inputs, double *const *outputs) {
-    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
-    if (n < 0 || !inputs || !outputs) return fail(ROSENNA_ERR_ARG, "bad arguments");
-    const Plan &P = g_ctx.plan;
-    std::vector<std::vector<float>> fi(P.inputs.size()), fo(P.outputs.size());
-    std::vector<const float *> pi;
-    std::vector<float *> po;
-    for (size_t i = 0; i < P.inputs.size(); i++) {
-        if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
-        size_t cnt = (size_t)(P.inputs[i].rows * n);
-        fi[i].resize(cnt);
-        for (size_t k = 0; k < cnt; k++) fi[i][k] = (float)inputs[i][k];
-        pi.push_back(fi[i].data());
-    }
-    for (size_t i = 0; i < P.outputs.size(); i++) {
-        if (!outputs[i]) return fail(ROSENNA_ERR_ARG, "null output pointer");
-        fo[i].resize((size_t)(P.outputs[i].rows * n));
-        po.push_back(fo[i].data());
-    }
-    int rc = rosenna_use_model_f32(n, pi.data(), po.data());
-    if (rc) return rc;
-    for (size_t i = 0; i < P.outputs.size(); i++)
-        for (size_t k = 0; k < fo[i].size(); k++) outputs[i][k] = fo[i][k];
-    return ok();
+    std::lock_guard<std::mutex> lk(g_mu);
+    return use_model_f64_locked(n, inputs, outputs);
 }
 
 int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *const *outputs, void *stream) {
@@ -762,35 +830,112 @@ int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *c
     return ok();
 }
 
+int rosenna_step_timing_begin(int64_t max_records) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    if (max_records < 0 || max_records > ((int64_t)1 << 20)) return fail(ROSENNA_ERR_ARG, "max_records out of range");
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (auto &dp : g_ctx.devs) {
+        Device &d = *dp;
+        if (cudaSetDevice(d.id) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaSetDevice failed");
+        for (auto e : d.tev) cudaEventDestroy(e);
+        d.tev.assign((size_t)(2 * max_records), nullptr);
+        for (auto &e : d.tev)
+            if (cudaEventCreate(&e) != cudaSuccess) {
+                cudaSetDevice(cur);
+                return fail(ROSENNA_ERR_CUDA, "cudaEventCreate (step timing) failed");
+            }
+        d.tev_step.assign((size_t)max_records, -1);
+        d.tev_used = 0;
+    }
+    cudaSetDevice(cur);
+    return ok();
+}
+
+int rosenna_step_timing_end(double *ms, int64_t *runs, int max_steps) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    if (max_steps < 0 || (max_steps > 0 && (!ms || !runs))) return fail(ROSENNA_ERR_ARG, "bad step arrays");
+    for (int i = 0; i < max_steps; i++) {
+        ms[i] = 0.0;
+        runs[i] = 0;
+    }
+    int cur = 0;
+    cudaGetDevice(&cur);
+    int rc = 0;
+    for (auto &dp : g_ctx.devs) {
+        Device &d = *dp;
+        cudaSetDevice(d.id);
+        for (int64_t k = 0; k < d.tev_used && !rc; k++) {
+            float t = 0.f;
+            if (cudaEventSynchronize(d.tev[(size_t)(2 * k + 1)]) != cudaSuccess ||
+                cudaEventElapsedTime(&t, d.tev[(size_t)(2 * k)], d.tev[(size_t)(2 * k + 1)]) != cudaSuccess) {
+                rc = fail(ROSENNA_ERR_CUDA, "step timing events could not be read");
+                break;
+            }
+            const int si = d.tev_step[(size_t)k];
+            if (si >= 0 && si < max_steps) {
+                ms[si] += t;
+                runs[si]++;
+            }
+        }
+        for (auto e : d.tev) cudaEventDestroy(e);
+        d.tev.clear();
+        d.tev_step.clear();
+        d.tev_used = 0;
+    }
+    cudaSetDevice(cur);
+    return rc ? rc : ok();
+}
+
+int rosenna_step_count(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_ctx.ready ? (int)g_ctx.plan.steps.size() : -ROSENNA_ERR_STATE;
+}
+
+int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sample) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ctx.ready) return fail(ROSENNA_ERR_STATE, "initialize() has not succeeded");
+    if (i < 0 || i >= (int)g_ctx.plan.steps.size()) return fail(ROSENNA_ERR_ARG, "step index out of range");
+    const Step &s = g_ctx.plan.steps[(size_t)i];
+    std::string name;
+    double f = 0.0;
+    switch (s.kind) {
+        case Step::MLP: {
+            const bool dual = s.tc && !g_ctx.devs.empty() && g_ctx.devs[0]->tc_args[(size_t)i].dual;
+            name = s.tc ? (dual ? "mlp_tc_dual_kernel" : "mlp_tc_kernel") : "mlp_ffma_kernel";
+            for (auto &l : s.layers) f += 2.0 * l.K * l.M;
+            f *= s.rsub;
+            break;
+        }
+        case Step::LSTM:
+            name = s.tc ? "lstm_tc_kernel" : "lstm_ffma_kernel";
+            f = 2.0 * s.T * 4.0 * s.H * (double)(s.I + s.H);
+            break;
+        case Step::CONV: {
+            ConvArgs a{};
+            a.conv = s.conv; a.relu = s.relu; a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.OC = s.OC; a.KS = s.KS;
+            a.str_h = s.str_h; a.str_w = s.str_w; a.pool = s.pool; a.pk = s.pk;
+            name = conv_kernel_name(a);
+            if (s.conv) f = 2.0 * s.Ho * s.Wo * s.OC * (double)s.C * s.KS * s.KS;
+            break;
+        }
+        case Step::GATHER:
+        case Step::COPY: name = "gather_kernel"; break;
+        case Step::ACT:
+        case Step::ADD: name = "act_kernel"; break;
+    }
+    if (kernel && kernel_len > 0) snprintf(kernel, (size_t)kernel_len, "%s", name.c_str());
+    if (flops_per_sample) *flops_per_sample = f;
+    return ok();
+}
+
 int64_t rosenna_last_launch_count(void) { return g_launches.load(); }
 
 const char *rosenna_plan_description(void) { return g_ctx.desc.c_str(); }
 
 }  // extern "C"
-
-// ---------------------------------------------------------------------------
-// Allocation-free use_model on device arrays.
-//
-// Some callers cannot have the library allocate device memory while they run:
-// a solver that hands all free GPU memory to its own pool allocator at start-up
-// (cudaMalloc would then fail), or a time-step loop that must not stall, since
-// cudaMalloc/cudaFree synchronise the device.  rosenna_use_model_device_f32
-// allocates its intermediate buffers on first use; this entry point instead
-// carves them from one fixed array in device memory that every GPU loading
-// this library holds until the process exits.
-// ---------------------------------------------------------------------------
-namespace rosenna {
-namespace {
-
-constexpr size_t kNoAllocScratchBytes = (size_t)64 << 20;  // 64 MiB per GPU
-
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-
-// device address of g_noalloc_scratch per device id, looked up once per device
-std::vector<void *> g_noalloc_addr;
-
-}  // namespace
-}  // namespace rosenna
 
 extern "C" int rosenna_use_model_device_noalloc_f32(int64_t n, const float *const *inputs, float *const *outputs,
                                                     void *stream) {
@@ -840,16 +985,9 @@ extern "C" int rosenna_use_model_device_noalloc_f32(int64_t n, const float *cons
         ~Restore() { cudaSetDevice(dev); }
     } restore{cur};
     if (cudaSetDevice(d->id) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaSetDevice failed");
-    // set-up, once per device, with that device current
-    if ((int)g_noalloc_addr.size() <= d->id) g_noalloc_addr.resize((size_t)d->id + 1, nullptr);
-    if (!g_noalloc_addr[(size_t)d->id]) {
-        void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            return fail(ROSENNA_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
-        g_noalloc_addr[(size_t)d->id] = p;
-    }
-    unsigned char *base = static_cast<unsigned char *>(g_noalloc_addr[(size_t)d->id]);
+    // the array's device address was looked up at initialize, with this device current
+    if (!d->noalloc_base) return fail(ROSENNA_ERR_CUDA, d->noalloc_err);
+    unsigned char *base = static_cast<unsigned char *>(d->noalloc_base);
 
     std::vector<float *> ptr(P.buf_rows.size(), nullptr);
     std::vector<int64_t> ld(P.buf_rows.size(), n);

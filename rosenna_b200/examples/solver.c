@@ -3,7 +3,7 @@
  *   gcc solver.c -I<repo>/include -L<repo>/rosenna_b200 -lrosenna_b200 -Wl,-rpath,<repo>/rosenna_b200
  * and run it in a directory holding onnxModel.txt, onnxWeights.txt and
  * variables.fpp of a one-input, one-output model.  Prints the status and the
- * first outputs. */
+ * outputs of the first sample (all inputs 1, as torch.ones in goldenFiles). */
 #include <stdio.h>
 #include <stdlib.h>
 
@@ -31,7 +31,7 @@ int main(int argc, char **argv) {
     float *outs[1] = {y};
     rc = rosenna_use_model_f32(n, ins, outs);
     printf("use_model: status %d launches %lld\n", rc, (long long)rosenna_last_launch_count());
-    for (long long i = 0; i < out_rows && !rc; i++) printf("%.7g ", y[i * n]);
+    for (long long i = 0; i < out_rows && !rc; i++) printf("%.9g ", y[i * n]);
     printf("\n");
     free(x);
     free(y);

@@ -105,3 +105,46 @@ def max_over_ranks(x: float, group=None) -> float:
     t = torch.tensor([float(x)], dtype=torch.float64, device=_collective_device(group))
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+def _parse_cpulist(text: str) -> List[int]:
+    cpus: List[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.extend(range(int(a), int(b) + 1))
+        else:
+            cpus.append(int(part))
+    return cpus
+
+
+def bind_host_to_device(device: int) -> Optional[dict]:
+    """Restricts this process to the host CPUs of the NUMA node its GPU hangs
+    off (sysfs local_cpulist of the GPU's PCI device), so that pinned host
+    buffers allocated afterwards live on that node and host<->device copies do
+    not cross the inter-socket link.  Returns {"node", "cpus"} or None when the
+    topology cannot be read (the affinity is then left as it is)."""
+    try:
+        import torch
+
+        pr = torch.cuda.get_device_properties(device)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        base = os.path.join("/sys/bus/pci/devices", bus)
+        with open(os.path.join(base, "local_cpulist")) as f:
+            cpus = _parse_cpulist(f.read())
+        node = -1
+        try:
+            with open(os.path.join(base, "numa_node")) as f:
+                node = int(f.read().strip())
+        except (OSError, ValueError):
+            pass
+        allowed = set(os.sched_getaffinity(0))
+        cpus = [c for c in cpus if c in allowed]
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return {"node": node, "cpus": len(cpus)}
+    except Exception:
+        return None
