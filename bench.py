@@ -277,8 +277,10 @@ def measure(name, n, args, rank, local, world, want_cpu, fp32_ref):
     dom = max(range(len(step_times)), key=lambda i: step_times[i][0])
     kname, fps = steps_info[dom]
     k_ms, k_runs = step_times[dom]
-    k_s = k_ms / 1e3 / max(1, k_runs)
-    achieved = fps * n / k_s / 1e12 if fps > 0 else None
+    # a call may split the batch into chunks (intermediates beyond the scratch
+    # budget): the step then runs once per chunk; per call it processes all n samples
+    k_call_s = k_ms / 1e3 / max(1, args.steps)
+    achieved = fps * n / k_call_s / 1e12 if fps > 0 else None
     if "_tc" in kname:
         peak, src = tensor_peak()
         bound = "tensor"
@@ -292,7 +294,8 @@ def measure(name, n, args, rank, local, world, want_cpu, fp32_ref):
     per_sample = NCU_TRAFFIC_PER_SAMPLE.get((name, kname))
     roof = {"bound": bound, "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
             "frac": achieved / peak if achieved else None, "peak_source": src,
-            "kernel_ms_per_launch": k_s * 1e3, "kernel_share": k_ms / total_ms if total_ms else None,
+            "kernel_ms_per_call": k_call_s * 1e3, "launches_per_call": k_runs / max(1, args.steps),
+            "kernel_share": k_ms / total_ms if total_ms else None,
             "algorithmic_flops_per_launch": fps * n,
             "traffic": per_sample * n if per_sample else None,
             "traffic_unit": "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, per sample x batch)",

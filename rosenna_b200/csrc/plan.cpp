@@ -257,6 +257,7 @@ class Builder {
     Status op_reshape(const PyVal &e);
     Status op_squeeze(const PyVal &e);
     Status finish();
+    void fold_gathers_into_convs();
 };
 
 // Appends Y = X . W^T + bias (W[m][k] = w_mk[m + M*k], the Fortran (M,K)
@@ -819,7 +820,55 @@ Status Builder::finish() {
     }
     std::reverse(kept.begin(), kept.end());
     plan_->steps = kept;
+    fold_gathers_into_convs();
     return Status::Ok();
+}
+
+// A gather that only permutes the rows a conv/pool step just wrote (the C-order
+// flatten of a (C, H, W) result, modelCreator.fpp:122-130) folds into that
+// step: the kernels write output row c*so_c + h*so_h + w*so_w, so when the
+// permutation maps (c, h, w) affinely the step writes the gathered order
+// directly and the gather pass goes away.
+void Builder::fold_gathers_into_convs() {
+    auto &steps = plan_->steps;
+    for (size_t i = 1; i < steps.size(); i++) {
+        Step &g = steps[i], &c = steps[i - 1];
+        if (g.kind != Step::GATHER || c.kind != Step::CONV || c.out != g.in) continue;
+        bool other_reader = false;
+        for (size_t k = 0; k < steps.size(); k++)
+            if (k != i && (steps[k].in == c.out || steps[k].h0 == c.out || steps[k].c0 == c.out)) other_reader = true;
+        for (auto *v : {&plan_->inputs, &plan_->outputs})
+            for (auto &io : *v)
+                if (io.buf == c.out) other_reader = true;
+        const int64_t rows = plan_->buf_rows[(size_t)g.out];
+        if (other_reader || rows != plan_->buf_rows[(size_t)c.out] || rows != (int64_t)c.OC * c.Hq * c.Wq) continue;
+        const int32_t *map = reinterpret_cast<const int32_t *>(plan_->arena.data() + g.map_off);
+        std::vector<int64_t> inv((size_t)rows, -1);
+        bool perm = true;
+        for (int64_t r = 0; r < rows && perm; r++) {
+            const int64_t src = map[r];
+            if (src < 0 || src >= rows || inv[(size_t)src] >= 0) perm = false;
+            else inv[(size_t)src] = r;
+        }
+        if (!perm) continue;
+        auto old_row = [&](int64_t ch, int64_t h, int64_t w) { return ch * c.so_c + h * c.so_h + w * c.so_w; };
+        const int64_t r0 = inv[(size_t)old_row(0, 0, 0)];
+        const int64_t sc = c.OC > 1 ? inv[(size_t)old_row(1, 0, 0)] - r0 : 1;
+        const int64_t sh = c.Hq > 1 ? inv[(size_t)old_row(0, 1, 0)] - r0 : 1;
+        const int64_t sw = c.Wq > 1 ? inv[(size_t)old_row(0, 0, 1)] - r0 : 1;
+        bool affine = r0 == 0;
+        for (int64_t ch = 0; ch < c.OC && affine; ch++)
+            for (int64_t h = 0; h < c.Hq && affine; h++)
+                for (int64_t w = 0; w < c.Wq && affine; w++)
+                    affine = inv[(size_t)old_row(ch, h, w)] == ch * sc + h * sh + w * sw;
+        if (!affine) continue;
+        c.so_c = sc;
+        c.so_h = sh;
+        c.so_w = sw;
+        c.out = g.out;
+        steps.erase(steps.begin() + (std::ptrdiff_t)i);
+        i--;
+    }
 }
 
 Status Builder::run() {

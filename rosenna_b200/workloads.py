@@ -24,7 +24,6 @@ import torch
 import torch.nn as nn
 
 from . import writer
-from .writer import View
 
 
 @dataclass
@@ -132,7 +131,7 @@ def _cnn():
     f1, f2 = nn.Linear(784, 64), nn.Linear(64, 10)
     for m in (c1, c2, f1, f2):
         nn.init.kaiming_uniform_(m.weight, nonlinearity="relu")
-    mods = [c1, nn.ReLU(), nn.MaxPool2d(2, 2), c2, nn.ReLU(), nn.AvgPool2d(2, 2), View(1, -1), f1, nn.ReLU(), f2]
+    mods = [c1, nn.ReLU(), nn.MaxPool2d(2, 2), c2, nn.ReLU(), nn.AvgPool2d(2, 2), nn.Flatten(), f1, nn.ReLU(), f2]
     return writer.export_sequential(mods, [1, 1, 28, 28]), nn.Sequential(*mods)
 
 

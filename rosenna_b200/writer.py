@@ -232,6 +232,22 @@ def write_model_files(g: Graph, out_dir: str) -> None:
             inputs.append(["output" + extra, len(inter[node.outputs[0]])])
             io_map[node.outputs[0]] = "output" + extra
             extra = str(int(extra) + 1)
+        elif layer == "Flatten":
+            # modelParserONNX.py:519-523 writes nothing for Flatten and passes its
+            # input through, so a Gemm after it would get the 4-D array; here it is
+            # written as the variable-form Reshape entry that x.view(N, -1) gives
+            # (:312-331), to the 2-D shape ONNX defines for Flatten(axis)
+            f_lines.append("Reshape")
+            src = node.inputs[0]
+            src_shape = list(inter.get(src, input_shapes.get(src, [])))
+            axis = int(node.attrs.get("axis", 1))
+            axis = axis + len(src_shape) if axis < 0 else axis
+            new_shape = [int(np.prod(src_shape[:axis])), int(np.prod(src_shape[axis:]))]
+            arch.append(("Reshape", (io_map[src], len(src_shape)), ["output" + extra], [new_shape], [0]))
+            f_lines.append("0")
+            inputs.append(["output" + extra, 2])
+            io_map[node.outputs[0]] = "output" + extra
+            extra = str(int(extra) + 1)
         elif layer == "Conv":  # :333-390
             f_lines.append(layer)
             attributes = dict(node.attrs)
@@ -414,6 +430,13 @@ def _emit_module(b: _Builder, mod, x: str, shape: List[int]) -> Tuple[str, List[
         attrs = {"ceil_mode": 0, "kernel_shape": [k, k], "pads": [p, p, p, p], "strides": [s, s]}
         (y,) = b.add(op, [x], [out_shape], attrs)
         return y, out_shape
+    if isinstance(mod, nn.Flatten):
+        a = mod.start_dim if mod.start_dim >= 0 else mod.start_dim + len(shape)
+        if mod.end_dim not in (-1, len(shape) - 1):
+            raise TypeError("only Flatten up to the last dimension exports as ONNX Flatten")
+        out_shape = [int(np.prod(shape[:a])), int(np.prod(shape[a:]))]
+        (y,) = b.add("Flatten", [x], [out_shape], {"axis": a})
+        return y, out_shape
     if isinstance(mod, View):
         target = list(mod.shape)
         tgt = _reshape_parser(target, shape)
@@ -437,7 +460,7 @@ class View(__import__("torch").nn.Module):
 
 
 def export_sequential(modules: Sequence, input_shape: Sequence[int]) -> Graph:
-    """Graph of a feed-forward stack (Linear/act/Conv/pool/View) with one input."""
+    """Graph of a feed-forward stack (Linear/act/Conv/pool/Flatten/View) with one input."""
     b = _Builder()
     x, shape = "input", list(input_shape)
     for m in modules:

@@ -39,7 +39,10 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from rosenna_b200 import onnx_file, writer  # noqa: E402
 from rosenna_b200.writer import Graph, Node, View  # noqa: E402
 
-REFERENCE_MNIST = "/root/reference/goldenFiles/mnist"
+# the roseNNa checkout (its goldenFiles/mnist holds the one stored model);
+# ROSENNA_REFERENCE_DIR names it, the mnist case is skipped without it
+REFERENCE_DIR = os.environ.get("ROSENNA_REFERENCE_DIR", "")
+REFERENCE_MNIST = os.path.join(REFERENCE_DIR, "goldenFiles", "mnist") if REFERENCE_DIR else ""
 
 
 def _line(vals):
@@ -182,7 +185,7 @@ def stored_model_case(name, g, inputs):
 def mnist_case():
     import re
 
-    if not os.path.isdir(REFERENCE_MNIST):
+    if not REFERENCE_MNIST or not os.path.isdir(REFERENCE_MNIST):
         print("mnist: reference tree absent, committed fixture kept")
         return
     g = onnx_file.load_graph(os.path.join(REFERENCE_MNIST, "mnist.onnx"))

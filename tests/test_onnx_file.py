@@ -111,11 +111,14 @@ def _graphs():
                                    [1, 1, 8, 8])
     lstm = writer.export_lstm([nn.LSTM(4, 5, 1, batch_first=True)], [nn.Linear(5, 2)], 1, 6, mode="hn_head",
                               with_state=True)
-    return {"mlp": mlp, "cnn": cnn, "lstm": lstm}
+    torch.manual_seed(6)
+    cnn_flatten = writer.export_sequential([nn.Conv2d(1, 4, 3, padding=1), nn.ReLU(), nn.MaxPool2d(2, 2),
+                                            nn.Flatten(), nn.Linear(64, 3)], [1, 1, 8, 8])
+    return {"mlp": mlp, "cnn": cnn, "lstm": lstm, "cnn_flatten": cnn_flatten}
 
 
 @pytest.mark.parametrize("raw", [True, False])
-@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm"])
+@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm", "cnn_flatten"])
 def test_decoded_graph_writes_the_same_files(name, raw, tmp_path):
     g = _graphs()[name]
     (tmp_path / "m.onnx").write_bytes(encode(g, raw=raw))
@@ -130,7 +133,7 @@ def test_decoded_graph_writes_the_same_files(name, raw, tmp_path):
     assert _files(tmp_path / "direct") == _files(tmp_path / "decoded")
 
 
-@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm"])
+@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm", "cnn_flatten"])
 def test_shape_inference_recovers_value_info(name, tmp_path):
     g = _graphs()[name]
     (tmp_path / "m.onnx").write_bytes(encode(g, with_value_info=False))
@@ -167,9 +170,14 @@ def test_truncated_file_is_an_error():
         onnx_file.OnnxModel(encode(_graphs()["mlp"])[:-7])
 
 
-@pytest.mark.skipif(not os.path.isdir("/root/reference/goldenFiles/mnist"), reason="reference tree absent")
+# the roseNNa checkout, named by ROSENNA_REFERENCE_DIR (the test skips without it)
+REFERENCE_MNIST = os.path.join(os.environ.get("ROSENNA_REFERENCE_DIR", ""), "goldenFiles", "mnist")
+
+
+@pytest.mark.skipif(not os.environ.get("ROSENNA_REFERENCE_DIR") or not os.path.isdir(REFERENCE_MNIST),
+                    reason="ROSENNA_REFERENCE_DIR does not name a roseNNa checkout")
 def test_mnist_onnx_decodes_to_the_committed_fixture(tmp_path):
-    g = onnx_file.load_graph("/root/reference/goldenFiles/mnist/mnist.onnx")
+    g = onnx_file.load_graph(os.path.join(REFERENCE_MNIST, "mnist.onnx"))
     writer.write_model_files(g, str(tmp_path))
     assert _files(tmp_path) == _files(goldens.case_dir("mnist"))
 
@@ -180,3 +188,23 @@ def test_command_line_writes_the_three_files(tmp_path):
     onnx_file.main(["-f", str(tmp_path / "m.onnx"), "-o", str(tmp_path / "out")])
     writer.write_model_files(g, str(tmp_path / "direct"))
     assert _files(tmp_path / "out") == _files(tmp_path / "direct")
+
+
+def test_flatten_writes_the_files_of_a_view(tmp_path):
+    """nn.Flatten (ONNX Flatten, which modelParserONNX.py:519-523 passes through
+    unwritten) is written as the variable-form Reshape entry x.view(N, -1) gives:
+    the same variables.fpp and weights; onnxModel.txt differs only by the view's
+    Constant node (its node count and its name line)."""
+    import torch
+
+    def stack(flat):
+        torch.manual_seed(9)
+        mods = [nn.Conv2d(2, 3, 3, padding=1), nn.ReLU(), nn.AvgPool2d(2, 2)]
+        return mods + [nn.Flatten() if flat else View(1, -1), nn.Linear(27, 4)]
+
+    writer.write_model_files(writer.export_sequential(stack(True), [1, 2, 6, 6]), str(tmp_path / "f"))
+    writer.write_model_files(writer.export_sequential(stack(False), [1, 2, 6, 6]), str(tmp_path / "v"))
+    f, v = _files(tmp_path / "f"), _files(tmp_path / "v")
+    assert f["variables.fpp"] == v["variables.fpp"] and f["onnxWeights.txt"] == v["onnxWeights.txt"]
+    fl, vl = f["onnxModel.txt"].splitlines(), v["onnxModel.txt"].splitlines()
+    assert int(vl[0]) == int(fl[0]) + 1 and [x for x in vl[1:] if x != "Constant"] == fl[1:]
