@@ -201,13 +201,13 @@ def oracle_leg(name, model_dir, host_in, outs_by_path, target_seconds):
     idx0 = parity.check_indices(n, 512, seed=w_key)
     sub = [np.ascontiguousarray(x[:, idx0], dtype=np.float64) for x in host_in]
     t0 = time.perf_counter()
-    m.run_batched(len(idx0), sub, [1] * len(sub), [1], threads)
+    m.run_batched(len(idx0), sub, threads=threads)
     rate = len(idx0) / max(time.perf_counter() - t0, 1e-6)
     count = int(min(n, max(4096, rate * target_seconds)))
     idx = parity.check_indices(n, count, seed=w_key)
     sub = [np.ascontiguousarray(x[:, idx], dtype=np.float64) for x in host_in]
     t0 = time.perf_counter()
-    ref = m.run_batched(len(idx), sub, [1] * len(sub), [1], threads)[0].reshape(-1, len(idx))
+    ref = m.run_batched(len(idx), sub, threads=threads)[0].reshape(-1, len(idx))
     dt = time.perf_counter() - t0
     par = {"samples_checked": int(len(idx)), "limits": {"max_abs": parity.ABS_TOL, "max_rel": parity.REL_TOL,
                                                         "rel_where_abs_ref_ge": parity.REL_FLOOR}}
@@ -371,14 +371,14 @@ def run_reference(args):
             k = max(64, threads * 8)
             ins = workloads.make_inputs(name, k, seed_offset=99)
             t0 = time.perf_counter()
-            m.run_batched(k, ins, [1] * len(ins), [1], threads)
+            m.run_batched(k, ins, threads=threads)
             rate = k / max(time.perf_counter() - t0, 1e-6)
             k = int(max(threads, min(1 << 22, rate * seconds)))
             ins = workloads.make_inputs(name, k, seed_offset=98)
             rates = []
             for _ in range(steps):
                 t0 = time.perf_counter()
-                m.run_batched(k, ins, [1] * len(ins), [1], threads)
+                m.run_batched(k, ins, threads=threads)
                 rates.append(k / (time.perf_counter() - t0))
         return {"value": statistics.median(rates), "unit": "samples/s", "cores": threads, "kind": "port",
                 "sample": f"{k} samples of the workload per step (batch {w.batch}), fp64, use_model once per "

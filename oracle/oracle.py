@@ -72,6 +72,30 @@ class OracleModel:
         for i in range(lib.ro_num_outputs(self._h)):
             r = lib.ro_output_shape(self._h, i, dims)
             self.output_shapes.append(tuple(dims[j] for j in range(r)))
+        self.input_pre = self._input_pre(os.path.join(model_dir, "variables.fpp"))
+
+    def _input_pre(self, variables_fpp):
+        """Elements in front of each input's batch index in the reference layout:
+        the batch is dim 1 of an input first read by an LSTM ((T, N, I) and
+        (1, N, H) forms) or a Slice (a stacked LSTM's (L, N, H) state), else dim 0."""
+        import ast
+
+        first = {}
+        with open(variables_fpp) as f:
+            for line in f:
+                if line.startswith("#:set architecture"):
+                    for e in ast.literal_eval(line.split("=", 1)[1].strip()):
+                        names = e[1] if isinstance(e[1], (list, tuple)) else []
+                        for nm in names:
+                            if isinstance(nm, str) and nm not in first:
+                                first[nm] = e[0]
+        with open(variables_fpp) as f:
+            true_inputs = [ast.literal_eval(ln.split("=", 1)[1].strip()) for ln in f if ln.startswith("#:set trueInputs")][0]
+        pre = []
+        for name, shape in true_inputs:
+            b = 1 if first.get(name) in ("LSTM", "Slice") and len(shape) >= 2 else 0
+            pre.append(int(np.prod(shape[:b])) if b else 1)
+        return pre
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -89,14 +113,20 @@ class OracleModel:
             raise RuntimeError("oracle run failed: " + err.value.decode())
         return outs
 
-    def run_batched(self, n, inputs, in_pre, out_pre, threads=None):
+    def run_batched(self, n, inputs, in_pre=None, out_pre=None, threads=None):
         """Per-sample loop over a batch of n (model exported at batch 1), on
         `threads` OpenMP threads (default: every host core this process may use).
 
-        `inputs` are flat float64 arrays in the batched reference layout; returns
-        flat float64 outputs in the same layout."""
+        `inputs` are float64 arrays in the batched reference layout (any shape
+        holding that memory order); in_pre / out_pre give the elements in front
+        of each array's batch index (default: from the model); returns flat
+        float64 outputs in the reference layout."""
         if threads is None:
             threads = host_cores()
+        if in_pre is None:
+            in_pre = self.input_pre
+        if out_pre is None:
+            out_pre = [1] * len(self.output_shapes)
         ins = [np.ascontiguousarray(x, dtype=np.float64).reshape(-1) for x in inputs]
         outs = [np.zeros(int(np.prod(s)) * n, dtype=np.float64) for s in self.output_shapes]
         ip = (ctypes.c_int * len(in_pre))(*in_pre)

@@ -932,6 +932,98 @@ static int run_op(const ro_model *m, Vars *vs, const PV *tup, Counters *cnt, cha
         const Arr *y = var_get(vs, pv_str(pv_at(a1, 1)));
         const int rank = (int)pv_int(pv_at(a2, 0));
         if (!x || !y || matmul_nd(x, y, rank)) { set_err(err, errlen, "MatMul: bad operands"); return -1; }
+    } else if (!strcmp(op, "Slice") || !strcmp(op, "Gather")) {
+        /* ONNX Slice (axes, starts, ends; step 1) and Gather (axis, one index,
+         * the axis dropped).  modelParserONNX.py:519-523 writes nothing for
+         * these ops; this build's front end writes them as architecture entries
+         * (a stacked LSTM's per-layer initial states and the last layer's h_n). */
+        const int is_gather = op[0] == 'G';
+        Arr *x = var_get(vs, pv_str(pv_at(a1, 0)));
+        const char *on = pv_str(pv_at(a2, 0));
+        if (!x || !on) { set_err(err, errlen, "%s: missing input", op); return -1; }
+        int lo[MAXR], hi[MAXR];
+        for (int i = 0; i < x->rank; i++) { lo[i] = 0; hi[i] = x->d[i]; }
+        int drop = -1;
+        if (is_gather) {
+            int ax = (int)pv_int(pv_at(a3, 0)), idx = (int)pv_int(pv_at(a3, 1));
+            if (ax < 0) ax += x->rank;
+            if (ax < 0 || ax >= x->rank) { set_err(err, errlen, "Gather: bad axis"); return -1; }
+            if (idx < 0) idx += x->d[ax];
+            if (idx < 0 || idx >= x->d[ax]) { set_err(err, errlen, "Gather: index out of range"); return -1; }
+            lo[ax] = idx;
+            hi[ax] = idx + 1;
+            drop = ax;
+        } else {
+            int axes[MAXR], st[MAXR], en[MAXR];
+            const int na = pv_ints(pv_at(a3, 0), axes, MAXR), ns = pv_ints(pv_at(a3, 1), st, MAXR),
+                      ne = pv_ints(pv_at(a3, 2), en, MAXR);
+            if (na < 0 || na != ns || na != ne) { set_err(err, errlen, "Slice: bad parameters"); return -1; }
+            for (int j = 0; j < na; j++) {
+                int ax = axes[j] < 0 ? axes[j] + x->rank : axes[j];
+                if (ax < 0 || ax >= x->rank) { set_err(err, errlen, "Slice: bad axis"); return -1; }
+                int a = st[j] < 0 ? st[j] + x->d[ax] : st[j], b = en[j] < 0 ? en[j] + x->d[ax] : en[j];
+                a = a < 0 ? 0 : (a > x->d[ax] ? x->d[ax] : a);
+                b = b < a ? a : (b > x->d[ax] ? x->d[ax] : b);
+                lo[ax] = a;
+                hi[ax] = b;
+            }
+        }
+        int od[MAXR], orank = 0;
+        for (int i = 0; i < x->rank; i++)
+            if (i != drop) od[orank++] = hi[i] - lo[i];
+        int full[MAXR];
+        for (int i = 0; i < x->rank; i++) full[i] = hi[i] - lo[i];
+        Arr o = arr_new(orank, od);
+        const int64_t n = arr_numel(&o);
+        for (int64_t L = 0; L < n; L++) {  /* column-major walk of the kept box */
+            int64_t rem = L, src = 0, stride = 1;
+            for (int i = 0; i < x->rank; i++) {
+                const int64_t k = rem % full[i];
+                rem /= full[i];
+                src += (k + lo[i]) * stride;
+                stride *= x->d[i];
+            }
+            o.v[L] = x->v[src];
+        }
+        var_set(vs, on, o);
+    } else if (!strcmp(op, "Concat")) {
+        /* ONNX Concat along `axis` (no reference counterpart: see Slice) */
+        const char *on = pv_str(pv_at(a2, 0));
+        int ax = (int)pv_int(pv_at(a3, 0));
+        const int k = a1 ? a1->n : 0;
+        Arr *parts[16];
+        if (k < 1 || k > 16 || !on) { set_err(err, errlen, "Concat: bad operands"); return -1; }
+        for (int j = 0; j < k; j++) {
+            parts[j] = var_get(vs, pv_str(pv_at(a1, j)));
+            if (!parts[j]) { set_err(err, errlen, "Concat: missing input"); return -1; }
+        }
+        const int r = parts[0]->rank;
+        if (ax < 0) ax += r;
+        if (ax < 0 || ax >= r) { set_err(err, errlen, "Concat: bad axis"); return -1; }
+        int od[MAXR];
+        for (int i = 0; i < r; i++) od[i] = parts[0]->d[i];
+        od[ax] = 0;
+        for (int j = 0; j < k; j++) {
+            for (int i = 0; i < r; i++)
+                if (i != ax && (parts[j]->rank != r || parts[j]->d[i] != od[i])) {
+                    set_err(err, errlen, "Concat: shapes differ");
+                    return -1;
+                }
+            od[ax] += parts[j]->d[ax];
+        }
+        Arr o = arr_new(r, od);
+        int64_t inner = 1, outer = 1;
+        for (int i = 0; i < ax; i++) inner *= od[i];
+        for (int i = ax + 1; i < r; i++) outer *= od[i];
+        for (int64_t q = 0; q < outer; q++) {
+            int64_t base = 0;
+            for (int j = 0; j < k; j++) {
+                const int64_t blk = inner * parts[j]->d[ax];
+                memcpy(o.v + q * inner * od[ax] + base, parts[j]->v + q * blk, sizeof(double) * (size_t)blk);
+                base += blk;
+            }
+        }
+        var_set(vs, on, o);
     } else if (!strcmp(op, "Relu") || !strcmp(op, "Tanh") || !strcmp(op, "Sigmoid")) { /* modelCreator.fpp:151-161 */
         Arr *x = var_get(vs, pv_str(pv_at(a1, 0)));
         if (!x) { set_err(err, errlen, "%s: missing input", op); return -1; }

@@ -571,6 +571,17 @@ __global__ void __launch_bounds__(128) conv_pool_kernel(const ConvArgs p) {
 }
 
 // ---- data movement / elementwise ------------------------------------------------
+// A model input whose batch index is not its first (reference layout: element
+// (p, s, q) of shape (pre.., n, post..) at p + pre*s + pre*ld_in*q) into the
+// plan's row layout (row p + pre*q, samples contiguous).
+__global__ void deinterleave_kernel(const float *in, long long ld_in, float *out, long long ld_out, int pre,
+                                    long long n) {
+    const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    const int r = blockIdx.y, p = r % pre, q = r / pre;
+    out[(long long)r * ld_out + s] = in[(long long)q * pre * ld_in + (long long)pre * s + p];
+}
+
 __global__ void gather_kernel(const float *in, long long ld_in, float *out, long long ld_out, const int *map, long long n) {
     const long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
@@ -731,6 +742,15 @@ cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st) {
     if (outs > 65535) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((a.n + 127) / 128), (unsigned)outs);
     conv_pool_kernel<<<grid, 128, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_deinterleave(const float *in, long long ld_in, float *out, long long ld_out, int pre, long long rows,
+                                long long n, cudaStream_t st) {
+    if (n <= 0 || rows <= 0) return cudaSuccess;
+    if (rows > 65535 || pre < 1) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)((n + 255) / 256), (unsigned)rows);
+    deinterleave_kernel<<<grid, 256, 0, st>>>(in, ld_in, out, ld_out, pre, n);
     return cudaGetLastError();
 }
 

@@ -68,6 +68,10 @@ cudaError_t launch_conv(const ConvArgs &a, cudaStream_t st);
 const char *conv_kernel_name(const ConvArgs &a);
 cudaError_t launch_gather(const float *in, long long ld_in, float *out, long long ld_out, const int *map, long long rows,
                           long long n, cudaStream_t st);
+// rows of a model input whose batch index is not its first (pre = product of
+// the dims in front of it): reference layout -> row p + pre*q
+cudaError_t launch_deinterleave(const float *in, long long ld_in, float *out, long long ld_out, int pre, long long rows,
+                                long long n, cudaStream_t st);
 // add: per-row constant added before the activation, or nullptr
 cudaError_t launch_act(const float *in, long long ld_in, float *out, long long ld_out, long long rows, long long n,
                        int act, const float *add, cudaStream_t st);

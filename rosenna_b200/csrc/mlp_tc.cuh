@@ -64,6 +64,32 @@ struct TcLstmArgs {
     int T, I, H, Np, nx, nh;  // nx / nh: K chunks of 32 of the x / h parts
 };
 
+// Two stacked LSTM layers with hidden size 64 (4H = 256) and layer-1 input
+// width <= 32, fused in one kernel (lstm2_tc.cu): layer 2 reads layer 1's h_t
+// from shared memory.  The blocks are the per-layer tensor-core blocks
+// ([2*256][Kp], Kp = 96 and 128), read through maps with boxes of {32, 128}.
+struct TcLstm2Args {
+    CUtensorMap map1, map2;
+    const float *arena;
+    long long h0_const[2], c0_const[2];  // per-unit constant initial state or -1
+    const float *x;
+    long long ld_x;                      // row t + T*i
+    const float *h0[2];
+    long long ld_h0[2];
+    const float *c0[2];
+    long long ld_c0[2];
+    float *y2;                           // layer 2's output sequence (row t + T*j) or null
+    long long ld_y2;
+    float *hn[2];
+    long long ld_hn[2];
+    float *cn[2];
+    long long ld_cn[2];
+    long long n;
+    int *err;
+    int T, I;
+    float bias1[256], bias2[256];        // b_ih + b_hh per gate column
+};
+
 size_t mlp_tc_smem_bytes();
 // The tensor-core kernels redistribute their launch registers between roles
 // (setmaxnreg) and only run when the compiler gave them exactly the count that
@@ -74,8 +100,14 @@ cudaError_t mlp_tc_configure();
 cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st);
 cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
 
-// Encodes the TMA map of one layer block at `block` (device pointer).
-// Returns false (with *why set) when the driver entry point or encode fails.
-bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, const char **why);
+// Encodes the TMA map of one layer block at `block` (device pointer), with
+// boxes of {32, box_rows} (box_rows 0: Np).  Returns false (with *why set) when
+// the driver entry point or encode fails.
+bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, const char **why, int box_rows = 0);
+
+// The fused two-layer LSTM kernel.
+bool lstm2_tc_regs_ok();
+cudaError_t lstm2_tc_configure();
+cudaError_t launch_lstm2_tc(const TcLstm2Args &a, int num_sms, cudaStream_t st);
 
 }  // namespace rosenna

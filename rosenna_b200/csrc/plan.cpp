@@ -24,6 +24,7 @@
 #include <sstream>
 
 #include "../../include/rosenna.h"
+#include "conv_tc.cuh"
 
 namespace rosenna {
 namespace {
@@ -154,7 +155,8 @@ bool is_identity(const std::vector<int32_t> &m, int64_t src_rows) {
 struct TVal {
     Shape shape;
     int bdim = 0;
-    int buf = -1;  // -2: value not representable per sample (an error if read); -3: a stored constant
+    int buf = -1;  // -2: value not representable per sample (an error if read); -3: a stored constant;
+                   // -4: a Concat, read only through a Slice/Gather selecting one of its parts
     int64_t rows() const { return numel(shape) / shape[(size_t)bdim]; }
 };
 
@@ -178,6 +180,7 @@ class Builder {
         return (int)plan_->buf_rows.size() - 1;
     }
     void bind(const std::string &name, const TVal &v) {
+        if (v.buf != -4) concats_.erase(name);
         auto it = vars_.find(name);
         if (it != vars_.end() && it->second.buf >= 0) refc_[(size_t)it->second.buf]--;
         if (v.buf >= 0) refc_[(size_t)v.buf]++;
@@ -188,6 +191,9 @@ class Builder {
         if (it == vars_.end()) return Status::Err(ROSENNA_ERR_FORMAT, "architecture reads undefined variable '" + name + "'");
         if (it->second.buf == -3)
             return Status::Err(ROSENNA_ERR_UNSUPPORTED, "variable '" + name + "' is a stored constant; only MatMul's second operand may be one");
+        if (it->second.buf == -4)
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED,
+                               "variable '" + name + "' is a Concat; it is read only through a Slice or Gather of one part");
         if (it->second.buf < 0)
             return Status::Err(ROSENNA_ERR_UNSUPPORTED, "variable '" + name + "' mixes samples after a Reshape; not batched");
         *v = it->second;
@@ -256,7 +262,11 @@ class Builder {
     Status op_transpose(const PyVal &e);
     Status op_reshape(const PyVal &e);
     Status op_squeeze(const PyVal &e);
+    Status op_slice(const PyVal &e, bool gather);
+    Status op_concat(const PyVal &e);
     Status finish();
+    void hoist_state_moves();
+    std::map<std::string, std::pair<int, std::vector<TVal>>> concats_;  // name -> (axis, parts)
     void fold_gathers_into_convs();
 };
 
@@ -605,6 +615,14 @@ Status Builder::op_conv(const PyVal &e) {  // modelCreator.fpp:103-105, layers.f
     for (int oc = 0; oc < s.OC; oc++) b[(size_t)oc] = (float)W.b.v[(size_t)oc];
     s.w_off = put(w.data(), w.size());
     s.b_off = put(b.data(), b.size());
+    if (s.KS == 3 && s.str_h == 1 && s.str_w == 1 && s.C <= 8 && s.OC <= 16) {
+        std::vector<float> img((size_t)kConvTcBFloatsTap);
+        conv_tc_pack(w.data(), s.OC, s.C, 0, img.data());
+        s.ctc_tap_off = put(img.data(), img.size());
+        img.assign((size_t)kConvTcBFloats, 0.f);
+        conv_tc_pack(w.data(), s.OC, s.C, 1, img.data());
+        s.ctc_win_off = put(img.data(), img.size());
+    }
     s.in = x.buf;
     s.out = new_buf((int64_t)s.OC * s.Ho * s.Wo);
     s.so_c = 1;
@@ -768,6 +786,124 @@ Status Builder::op_squeeze(const PyVal &e) {  // modelCreator.fpp:133-135
     return Status::Ok();
 }
 
+// ONNX Slice (axes/starts/ends, step 1) and Gather (one index, axis dropped),
+// written as architecture entries by this build's front end (the reference
+// parser passes them through, modelParserONNX.py:519-523): data movement
+// through a per-sample row map, or a whole part of a Concat.
+Status Builder::op_slice(const PyVal &e, bool gather) {
+    const std::string &xn = e.at(1).at(0).s, &on = e.at(2).at(0).s;
+    const PyVal &prm = e.at(3);
+    auto cit = concats_.find(xn);
+    std::vector<int64_t> axes, starts, ends;
+    if (gather) {
+        axes = {prm.at(0).as_int()};
+        starts = {prm.at(1).as_int()};
+        ends = {starts[0] + 1};
+    } else {
+        axes = prm.at(0).ints();
+        starts = prm.at(1).ints();
+        ends = prm.at(2).ints();
+        if (axes.size() != starts.size() || axes.size() != ends.size())
+            return Status::Err(ROSENNA_ERR_FORMAT, "Slice parameters");
+    }
+    TVal x;
+    if (cit != concats_.end()) {
+        // a selection of exactly one part of a Concat reads that part
+        const int cax = cit->second.first;
+        const auto &parts = cit->second.second;
+        const int rank = (int)parts[0].shape.size();
+        if (axes.size() != 1 || (axes[0] < 0 ? axes[0] + rank : axes[0]) != cax)
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED, "a Slice/Gather of a Concat must select along its axis");
+        int64_t total = 0;
+        for (auto &p : parts) total += p.shape[(size_t)cax];
+        int64_t a = starts[0] < 0 ? starts[0] + total : starts[0];
+        int64_t b = ends[0] < 0 ? ends[0] + total : std::min(ends[0], total);
+        if (gather) b = a + 1;
+        int64_t off = 0;
+        const TVal *hit = nullptr;
+        for (auto &p : parts) {
+            if (a == off && b == off + p.shape[(size_t)cax]) hit = &p;
+            off += p.shape[(size_t)cax];
+        }
+        if (!hit) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "a Slice/Gather of a Concat must select one whole part");
+        TVal v = *hit;
+        if (gather) {  // drop the (unit) axis
+            if (v.shape[(size_t)cax] != 1 || cax == v.bdim) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Gather of a Concat part");
+            v.shape.erase(v.shape.begin() + cax);
+            if (cax < v.bdim) v.bdim--;
+        }
+        concats_.erase(on);
+        bind(on, v);
+        return Status::Ok();
+    }
+    Status st = get(xn, &x);
+    if (!st.ok()) return st;
+    const int rank = (int)x.shape.size();
+    Shape lo(rank, 0), hi = x.shape;
+    for (size_t j = 0; j < axes.size(); j++) {
+        int ax = (int)(axes[j] < 0 ? axes[j] + rank : axes[j]);
+        if (ax < 0 || ax >= rank) return Status::Err(ROSENNA_ERR_FORMAT, "Slice axis");
+        if (ax == x.bdim) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Slice of the batch dimension");
+        int64_t d = x.shape[(size_t)ax];
+        int64_t a = starts[j] < 0 ? starts[j] + d : starts[j], b = ends[j] < 0 ? ends[j] + d : ends[j];
+        a = std::max<int64_t>(0, std::min(a, d));
+        b = std::max(a, std::min(b, d));
+        if (gather) b = a + 1;
+        if (b <= a) return Status::Err(ROSENNA_ERR_SHAPE, "empty Slice");
+        lo[(size_t)ax] = a;
+        hi[(size_t)ax] = b;
+    }
+    const int drop = gather ? (int)(axes[0] < 0 ? axes[0] + rank : axes[0]) : -1;
+    Shape S = probe(x), box(rank), R, Rx;
+    int b2 = x.bdim;
+    for (int i = 0; i < rank; i++) {
+        box[(size_t)i] = i == x.bdim ? S[(size_t)i] : hi[(size_t)i] - lo[(size_t)i];
+        if (i == drop) {
+            if (i < x.bdim) b2--;
+            continue;
+        }
+        R.push_back(box[(size_t)i]);
+        Rx.push_back(i == x.bdim ? x.shape[(size_t)i] : box[(size_t)i]);
+    }
+    // result element L (column-major over the box) <- source element at box index + lo
+    std::vector<int64_t> r2s((size_t)numel(box));
+    std::vector<int64_t> sub((size_t)rank);
+    for (int64_t L = 0; L < numel(box); L++) {
+        unravel(L, box, sub.data());
+        for (int i = 0; i < rank; i++) sub[(size_t)i] += i == x.bdim ? 0 : lo[(size_t)i];
+        r2s[(size_t)L] = ravel(sub.data(), S);
+    }
+    concats_.erase(on);
+    return move(on, x, Rx, R, b2, r2s, S, false);
+}
+
+// ONNX Concat (see op_slice): kept as its parts; only a Slice/Gather that
+// selects one whole part may read it (a stacked LSTM's h_n, read as h_n[-1]).
+Status Builder::op_concat(const PyVal &e) {
+    const std::string &on = e.at(2).at(0).s;
+    const int64_t axis = e.at(3).at(0).as_int();
+    std::vector<TVal> parts;
+    for (auto &n : e.at(1).items) {
+        TVal v;
+        Status st = get(n.s, &v);
+        if (!st.ok()) return st;
+        parts.push_back(v);
+    }
+    if (parts.empty()) return Status::Err(ROSENNA_ERR_FORMAT, "Concat without inputs");
+    const int rank = (int)parts[0].shape.size();
+    const int ax = (int)(axis < 0 ? axis + rank : axis);
+    Shape shape = parts[0].shape;
+    shape[(size_t)ax] = 0;
+    for (auto &p : parts) {
+        if ((int)p.shape.size() != rank || p.bdim != parts[0].bdim || ax == p.bdim)
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED, "Concat operands");
+        shape[(size_t)ax] += p.shape[(size_t)ax];
+    }
+    bind(on, TVal{shape, parts[0].bdim, -4});
+    concats_[on] = {ax, parts};
+    return Status::Ok();
+}
+
 Status Builder::finish() {
     const ModelFiles &m = mf_;
     // outputs: o<index> = outputs[<index>-th key]  (modelCreator.fpp:169-171)
@@ -821,7 +957,32 @@ Status Builder::finish() {
     std::reverse(kept.begin(), kept.end());
     plan_->steps = kept;
     fold_gathers_into_convs();
+    hoist_state_moves();
     return Status::Ok();
+}
+
+// A stacked LSTM's later layers take their initial state through data movement
+// (a Slice of the (L, N, H) state: a gather) issued between the layers.  Such
+// steps read nothing the earlier layer writes, so they move in front of it and
+// the two layers become adjacent (the runtime can then fuse them).
+void Builder::hoist_state_moves() {
+    auto &steps = plan_->steps;
+    for (size_t j = 0; j < steps.size(); j++) {
+        if (steps[j].kind != Step::LSTM) continue;
+        size_t k = j + 1;
+        while (k < steps.size() && (steps[k].kind == Step::GATHER || steps[k].kind == Step::COPY ||
+                                    steps[k].kind == Step::DEINTERLEAVE))
+            k++;
+        if (k == j + 1 || k >= steps.size() || steps[k].kind != Step::LSTM || steps[k].in != steps[j].y) continue;
+        bool independent = true;
+        for (size_t m = j + 1; m < k; m++)
+            for (int b : {steps[j].y, steps[j].hn, steps[j].cn})
+                if (b >= 0 && steps[m].in == b) independent = false;
+        if (!independent) continue;
+        std::rotate(steps.begin() + (std::ptrdiff_t)j, steps.begin() + (std::ptrdiff_t)j + 1,
+                    steps.begin() + (std::ptrdiff_t)k);
+        // steps j..k-2 are now the moves, k-1 the first LSTM, k the second
+    }
 }
 
 // A gather that only permutes the rows a conv/pool step just wrote (the C-order
@@ -874,7 +1035,8 @@ void Builder::fold_gathers_into_convs() {
 Status Builder::run() {
     const PyVal &arch = mf_.architecture;
     // batch dimension of each model input: 1 when the first entry that reads it
-    // is an LSTM (X is (T,N,I), h/c are (1,N,H)), else 0
+    // is an LSTM (X is (T,N,I), h/c are (1,N,H)) or a Slice (a stacked LSTM's
+    // (L,N,H) initial state), else 0
     std::set<std::string> lstm_operands, seen;
     for (auto &e : arch.items) {
         std::vector<std::string> names;
@@ -886,7 +1048,7 @@ Status Builder::run() {
         for (auto &n : names) {
             if (seen.count(n)) continue;
             seen.insert(n);
-            if (e.at(0).s == "LSTM") lstm_operands.insert(n);
+            if (e.at(0).s == "LSTM" || e.at(0).s == "Slice") lstm_operands.insert(n);
         }
     }
     for (size_t i = 0; i < mf_.true_inputs.size(); i++) {
@@ -898,12 +1060,21 @@ Status Builder::run() {
         int64_t b = d.shape[(size_t)d.bdim];
         if (i == 0) B0_ = b;
         else if (b != B0_) return Status::Err(ROSENNA_ERR_SHAPE, "inputs disagree on the export batch size");
-        for (int k = 0; k < d.bdim; k++)
-            if (d.shape[(size_t)k] != 1) return Status::Err(ROSENNA_ERR_UNSUPPORTED, "input with non-unit dims in front of its batch dimension");
+        d.pre = 1;
+        for (int k = 0; k < d.bdim; k++) d.pre *= d.shape[(size_t)k];
         d.rows = numel(d.shape) / b;
         d.buf = new_buf(d.rows);
         plan_->inputs.push_back(d);
-        bind(ti.at(0).s, TVal{d.shape, d.bdim, d.buf});
+        int vbuf = d.buf;
+        if (d.pre > 1) {  // samples are strided in the reference layout: rows of samples first
+            Step s;
+            s.kind = Step::DEINTERLEAVE;
+            s.in = d.buf;
+            s.out = vbuf = new_buf(d.rows);
+            s.pre = d.pre;
+            plan_->steps.push_back(s);
+        }
+        bind(ti.at(0).s, TVal{d.shape, d.bdim, vbuf});
     }
     plan_->export_batch = B0_;
     for (auto &e : arch.items) {
@@ -922,6 +1093,9 @@ Status Builder::run() {
         else if (op == "Transpose") st = op_transpose(e);
         else if (op == "Reshape") st = op_reshape(e);
         else if (op == "Squeeze") st = op_squeeze(e);
+        else if (op == "Slice") st = op_slice(e, false);
+        else if (op == "Gather") st = op_slice(e, true);
+        else if (op == "Concat") st = op_concat(e);
         else st = Status::Err(ROSENNA_ERR_UNSUPPORTED, "op " + op + " is not supported by the engine");
         if (!st.ok()) return st;
     }
@@ -939,7 +1113,10 @@ Status build_plan(const ModelFiles &mf, Plan *plan) {
 std::string Plan::describe() const {
     std::ostringstream o;
     static const char *acts[] = {"", "relu", "tanh", "sigmoid"};
-    for (auto &s : steps) {
+    for (size_t si = 0; si < steps.size(); si++) {
+        const Step &s = steps[si];
+        if (s.kind == Step::LSTM && s.fuse_next) o << "lstm2_tc (fused with the next step) ";
+        if (si > 0 && steps[si - 1].fuse_next) o << "(in lstm2_tc) ";
         switch (s.kind) {
             case Step::MLP:
                 o << (s.tc ? "mlp_tc b" : "mlp b") << s.in << "->b" << s.out << " [";
@@ -953,7 +1130,7 @@ std::string Plan::describe() const {
                   << s.c0 << " -> y=b" << s.y << " hn=b" << s.hn << " cn=b" << s.cn << "\n";
                 break;
             case Step::CONV:
-                o << (s.conv ? "conv" : "pool") << " b" << s.in << "->b" << s.out << " C=" << s.C << " " << s.Hin << "x"
+                o << (s.conv ? (s.tc ? "conv_tc" : "conv") : "pool") << " b" << s.in << "->b" << s.out << " C=" << s.C << " " << s.Hin << "x"
                   << s.Win;
                 if (s.conv) o << " OC=" << s.OC << " k=" << s.KS << " pad=" << s.pad_h << "," << s.pad_w << " s=" << s.str_h << "," << s.str_w;
                 if (s.relu) o << " relu";
@@ -964,6 +1141,7 @@ std::string Plan::describe() const {
             case Step::ACT: o << "act:" << acts[s.act] << " b" << s.in << "->b" << s.out << "\n"; break;
             case Step::ADD: o << "add" << (s.act ? "+" : "") << acts[s.act] << " b" << s.in << "->b" << s.out << "\n"; break;
             case Step::COPY: o << "copy b" << s.in << "->b" << s.out << "\n"; break;
+            case Step::DEINTERLEAVE: o << "deinterleave b" << s.in << "->b" << s.out << " pre=" << s.pre << "\n"; break;
         }
     }
     return o.str();

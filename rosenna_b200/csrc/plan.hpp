@@ -30,7 +30,7 @@ struct MlpLayer {
 };
 
 struct Step {
-    enum Kind { MLP, LSTM, CONV, GATHER, ACT, COPY, ADD } kind = MLP;
+    enum Kind { MLP, LSTM, CONV, GATHER, ACT, COPY, ADD, DEINTERLEAVE } kind = MLP;
     int in = -1, out = -1;  // buffer ids
 
     // MLP (also the head of an LSTM step); rsub sub-rows per sample (row k of
@@ -48,12 +48,18 @@ struct Step {
     // n = 4j+q (gate q of unit j) hi then lo, columns [x (nx chunks of 32) | h (nh)]
     int64_t lstm_tc_w_off = -1, lstm_tc_b_off = -1;
     int lstm_tc_Np = 0, lstm_tc_Kp = 0, lstm_tc_nx = 0, lstm_tc_nh = 0;
+    // this LSTM step and the next one (which reads only its y) run as one fused
+    // two-layer kernel; its y is never materialised (decided at initialize)
+    bool fuse_next = false;
 
     // CONV (+ReLU) (+pool); conv == false means pooling only
     bool conv = true, relu = false;
     int C = 0, Hin = 0, Win = 0, OC = 0, KS = 0, pad_h = 0, pad_w = 0, str_h = 1, str_w = 1, Ho = 0, Wo = 0;
     int pool = 0, pk = 1, ppad_h = 0, ppad_w = 0, pstr_h = 1, pstr_w = 1, Hq = 0, Wq = 0;  // pool: 0 none, 1 max, 2 avg
     int64_t so_c = 1, so_h = 0, so_w = 0;  // output row = oc*so_c + h*so_h + w*so_w
+    // tensor-core (implicit GEMM) B images of a 3x3 stride-1 conv with C <= 8
+    // and OC <= 16, per tap and per window (conv_tc.cuh); -1 when not packed
+    int64_t ctc_tap_off = -1, ctc_win_off = -1;
 
     // packed weights (MLP: per layer; LSTM/CONV: here)
     int64_t w_off = -1, b_off = -1;
@@ -62,12 +68,17 @@ struct Step {
     // act(in row r + arena[b_off + r])
     int64_t map_off = -1;
     int act = ACT_NONE;
+
+    // DEINTERLEAVE: a model input whose batch index is not the first (shape
+    // (p.., n, q..), `pre` = product of the dims in front): out row p + pre*q,
+    // sample s = in[q*pre*ld_in + pre*s + p] (the reference layout)
+    int64_t pre = 1;
 };
 
 struct IoDesc {
     std::vector<int64_t> shape;  // export shape
     int bdim = 0;
-    int64_t pre = 1;  // elements in front of the batch index; > 1 only at n == export batch
+    int64_t pre = 1;  // elements in front of the batch index (outputs: > 1 only at n == export batch)
     int64_t rows = 0;
     int buf = -1;
 };

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "../../include/rosenna.h"
+#include "conv_tc.cuh"
 #include "kernels.cuh"
 #include "mlp_tc.cuh"
 #include "model_files.hpp"
@@ -50,6 +51,7 @@ struct Device {
     int *err_host = nullptr;  // pinned copy, refreshed after each tensor-core launch
     std::vector<TcArgs> tc_args;  // per plan step (tensor-core MLP steps only)
     std::vector<TcLstmArgs> lstm_args;  // per plan step (tensor-core LSTM steps only)
+    std::vector<TcLstm2Args> lstm2_args;  // per plan step (first step of a fused LSTM pair only)
     Slot slots[kSlots];
     // allocation-free entry point: device address of the fixed scratch array,
     // looked up at initialize (or why it could not be)
@@ -73,6 +75,7 @@ struct Context {
     std::vector<int64_t> mlp_table_off;        // per step: index into mlp_tables, device offset in arena
     std::vector<int64_t> mlp_table_arena_off;
     std::vector<bool> is_io_in, is_io_out;
+    int conv_tc_mode = 1;  // tensor-core conv MMA form: 0 per tap (N = 16), 1 per window (N = 64)
 };
 
 Context g_ctx;
@@ -143,15 +146,29 @@ void release_all() {
 // intermediate buffers: used by a step and not a model input/output
 bool is_scratch(int b) { return !g_ctx.is_io_in[(size_t)b] && !g_ctx.is_io_out[(size_t)b]; }
 
+// Buffers the plan's launches touch.  A fused LSTM pair never writes the first
+// layer's output sequence (the second layer reads it from shared memory).
+std::vector<bool> used_buffers() {
+    const Plan &P = g_ctx.plan;
+    std::vector<bool> used(P.buf_rows.size(), false);
+    for (size_t si = 0; si < P.steps.size(); si++) {
+        const Step &st = P.steps[si];
+        const bool skip_y = st.kind == Step::LSTM && st.fuse_next;
+        const bool skip_in = si > 0 && P.steps[si - 1].fuse_next;
+        for (int b : {st.in, st.out, st.h0, st.c0, st.y, st.hn, st.cn}) {
+            if (b < 0 || (skip_y && b == st.y) || (skip_in && b == st.in)) continue;
+            used[(size_t)b] = true;
+        }
+    }
+    return used;
+}
+
 Status ensure_scratch(Slot &s, int64_t cap) {
     if (s.cap >= cap) return Status::Ok();
     for (auto p : s.scratch) cudaFree(p);
     s.scratch.assign(g_ctx.plan.buf_rows.size(), nullptr);
     s.cap = 0;
-    std::vector<bool> used(g_ctx.plan.buf_rows.size(), false);
-    for (auto &st : g_ctx.plan.steps)
-        for (int b : {st.in, st.out, st.h0, st.c0, st.y, st.hn, st.cn})
-            if (b >= 0) used[(size_t)b] = true;
+    const std::vector<bool> used = used_buffers();
     for (size_t b = 0; b < used.size(); b++) {
         if (!used[b] || !is_scratch((int)b)) continue;
         CUDA_TRY(cudaMalloc(&s.scratch[b], sizeof(float) * (size_t)g_ctx.plan.buf_rows[b] * (size_t)cap));
@@ -175,8 +192,9 @@ Status ensure_io(Slot &s, int64_t cap) {
 // Largest chunk whose intermediates fit the scratch budget.
 int64_t max_chunk(int64_t n) {
     int64_t rows = 0;
+    const std::vector<bool> used = used_buffers();
     for (size_t b = 0; b < g_ctx.plan.buf_rows.size(); b++)
-        if (is_scratch((int)b)) rows += g_ctx.plan.buf_rows[b];
+        if (used[b] && is_scratch((int)b)) rows += g_ctx.plan.buf_rows[b];
     int64_t cap = n;
     if (rows > 0) cap = std::max<int64_t>(1024, scratch_budget_bytes() / (int64_t)(sizeof(float) * rows));
     return std::max<int64_t>(1, std::min(cap, n));
@@ -230,6 +248,32 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 break;
             }
             case Step::LSTM: {
+                if (s.fuse_next) {
+                    const Step &s2 = P.steps[si + 1];
+                    TcLstm2Args &a = d.lstm2_args[si];
+                    a.x = ptr[(size_t)s.in];
+                    a.ld_x = ld[(size_t)s.in];
+                    const Step *ls[2] = {&s, &s2};
+                    for (int k = 0; k < 2; k++) {
+                        const Step &q = *ls[k];
+                        a.h0[k] = q.h0 >= 0 ? ptr[(size_t)q.h0] : nullptr;
+                        a.ld_h0[k] = q.h0 >= 0 ? ld[(size_t)q.h0] : 0;
+                        a.c0[k] = q.c0 >= 0 ? ptr[(size_t)q.c0] : nullptr;
+                        a.ld_c0[k] = q.c0 >= 0 ? ld[(size_t)q.c0] : 0;
+                        a.hn[k] = q.hn >= 0 ? ptr[(size_t)q.hn] : nullptr;
+                        a.ld_hn[k] = q.hn >= 0 ? ld[(size_t)q.hn] : 0;
+                        a.cn[k] = q.cn >= 0 ? ptr[(size_t)q.cn] : nullptr;
+                        a.ld_cn[k] = q.cn >= 0 ? ld[(size_t)q.cn] : 0;
+                    }
+                    a.y2 = s2.y >= 0 ? ptr[(size_t)s2.y] : nullptr;
+                    a.ld_y2 = s2.y >= 0 ? ld[(size_t)s2.y] : 0;
+                    a.n = cnt;
+                    e = launch_lstm2_tc(a, d.num_sms, stream);
+                    launches++;
+                    if (e == cudaSuccess)
+                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    break;
+                }
                 if (s.tc) {
                     TcLstmArgs a = d.lstm_args[si];
                     a.x = ptr[(size_t)s.in];
@@ -273,6 +317,27 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 break;
             }
             case Step::CONV: {
+                if (s.tc) {
+                    ConvTcArgs a{};
+                    a.arena = arena;
+                    a.bt_off = g_ctx.conv_tc_mode == 0 ? s.ctc_tap_off : s.ctc_win_off;
+                    a.b_off = s.b_off;
+                    a.in = ptr[(size_t)s.in];
+                    a.ld_in = ld[(size_t)s.in];
+                    a.out = ptr[(size_t)s.out];
+                    a.ld_out = ld[(size_t)s.out];
+                    a.so_c = s.so_c; a.so_h = s.so_h; a.so_w = s.so_w;
+                    a.n = cnt;
+                    a.err = d.err;
+                    a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.pad = s.pad_h; a.OC = s.OC;
+                    a.Hq = s.Hq; a.Wq = s.Wq; a.pool = s.pool; a.relu = s.relu ? 1 : 0;
+                    a.mode = g_ctx.conv_tc_mode;
+                    e = launch_conv_tc(a, d.num_sms, stream);
+                    launches++;
+                    if (e == cudaSuccess)
+                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    break;
+                }
                 ConvArgs a{};
                 a.arena = arena;
                 a.w_off = s.w_off;
@@ -302,6 +367,11 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 launches++;
                 break;
             }
+            case Step::DEINTERLEAVE:
+                e = launch_deinterleave(ptr[(size_t)s.in], ld[(size_t)s.in], ptr[(size_t)s.out], ld[(size_t)s.out],
+                                        (int)s.pre, P.buf_rows[(size_t)s.out], cnt, stream);
+                launches++;
+                break;
             case Step::ACT:
             case Step::ADD:
                 e = launch_act(ptr[(size_t)s.in], ld[(size_t)s.in], ptr[(size_t)s.out], ld[(size_t)s.out],
@@ -317,6 +387,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 return Status::Err(ROSENNA_ERR_CUDA, "cudaEventRecord (step timing) failed");
             d.tev_step[(size_t)d.tev_used++] = (int)si;
         }
+        if (s.kind == Step::LSTM && s.fuse_next) si++;  // the next layer ran inside the fused kernel
     }
     g_launches += launches;
     return Status::Ok();
@@ -351,11 +422,13 @@ Status check_batch(int64_t n) {
     if (n < 0) return Status::Err(ROSENNA_ERR_ARG, "negative batch size");
     Status st = check_device_status();
     if (!st.ok()) return st;
-    for (auto *v : {&g_ctx.plan.inputs, &g_ctx.plan.outputs})
-        for (auto &io : *v)
-            if (io.pre > 1 && n != 1)
-                return Status::Err(ROSENNA_ERR_UNSUPPORTED,
-                                   "an output merges the batch into another dimension; only n == 1 runs");
+    // inputs whose batch index is not the first are de-interleaved on the
+    // device; an output of that form (e.g. (N*T, H) from a Reshape that merges
+    // the batch into another dimension) mixes samples: only n == 1 runs
+    for (auto &io : g_ctx.plan.outputs)
+        if (io.pre > 1 && n != 1)
+            return Status::Err(ROSENNA_ERR_UNSUPPORTED,
+                               "an output merges the batch into another dimension; only n == 1 runs");
     return Status::Ok();
 }
 
@@ -399,10 +472,12 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
             ld[bi] = s.io.empty() || !s.io[bi] ? s.cap : s.io_cap;
         }
         for (size_t i = 0; i < P.inputs.size(); i++) {
+            // rows of `pre` interleaved samples' elements (pre = 1: rows of samples)
             const IoDesc &io = P.inputs[i];
-            CUDA_TRY(cudaMemcpy2DAsync(s.io[(size_t)io.buf], sizeof(float) * (size_t)s.io_cap, in[i] + c0,
-                                       sizeof(float) * (size_t)n, sizeof(float) * (size_t)cnt, (size_t)io.rows,
-                                       cudaMemcpyHostToDevice, s.stream));
+            const size_t pre = (size_t)io.pre;
+            CUDA_TRY(cudaMemcpy2DAsync(s.io[(size_t)io.buf], sizeof(float) * pre * (size_t)s.io_cap, in[i] + pre * c0,
+                                       sizeof(float) * pre * (size_t)n, sizeof(float) * pre * (size_t)cnt,
+                                       (size_t)io.rows / pre, cudaMemcpyHostToDevice, s.stream));
         }
         Status st = run_plan(d, ptr, ld, cnt, s.stream);
         if (!st.ok()) return st;
@@ -510,6 +585,48 @@ Status do_initialize(const std::string &model, const std::string &weights, const
     for (auto &s : P.steps)
         if (s.kind == Step::LSTM)
             s.tc = tc_ok && lstm_path != "ffma" && s.lstm_tc_w_off >= 0 && (lstm_path == "tc" || 4 * s.H > 128);
+    // two stacked LSTM layers with H = 64 (and a layer-1 input of at most 32)
+    // run as one fused kernel when the second layer is the only reader of the
+    // first layer's output sequence; ROSENNA_LSTM2_FUSE=0 keeps them apart
+    const char *fenv = getenv("ROSENNA_LSTM2_FUSE");
+    const bool fuse_ok = tc_ok && !(fenv && std::string(fenv) == "0") && lstm2_tc_regs_ok();
+    for (size_t si = 0; si + 1 < P.steps.size(); si++) {
+        Step &a = P.steps[si];
+        const Step &b = P.steps[si + 1];
+        a.fuse_next = false;
+        if (!fuse_ok || a.kind != Step::LSTM || b.kind != Step::LSTM || !a.tc || !b.tc || b.in != a.y || a.H != 64 ||
+            b.H != 64 || b.I != 64 || a.I > 32 || a.lstm_tc_Np != 256 || b.lstm_tc_Np != 256 || a.lstm_tc_Kp != 96 ||
+            b.lstm_tc_Kp != 128)
+            continue;
+        bool other_reader = false;
+        for (size_t k = 0; k < P.steps.size(); k++) {
+            const Step &q = P.steps[k];
+            if (k != si + 1 && (q.in == a.y || q.h0 == a.y || q.c0 == a.y)) other_reader = true;
+        }
+        for (auto *v : {&P.inputs, &P.outputs})
+            for (auto &io : *v)
+                if (io.buf == a.y) other_reader = true;
+        if (!other_reader) a.fuse_next = true;
+    }
+    // tensor-core conv (implicit GEMM) for the 3x3 stride-1 conv + 2x2 pool shapes
+    // it covers, with at least 4 input channels (a K-step holds 8 channels: fewer
+    // would multiply mostly zero padding; such convs stay on the CUDA cores);
+    // ROSENNA_CONV_PATH=tiled|direct keeps the CUDA-core kernels, =tc takes the
+    // tensor cores for every shape they cover; ROSENNA_CONV_TC_MODE=0|1 picks
+    // the MMA form
+    const char *cpath = getenv("ROSENNA_CONV_PATH");
+    const std::string conv_path = cpath ? cpath : "";
+    // (an M = 128 tcgen05 MMA of N <= 128 columns takes ~65 cycles whatever N,
+    // measured: the per-window form's 48 MMAs of N = 64 cost less than the
+    // per-tap form's 108 of N = 16)
+    const char *cmode = getenv("ROSENNA_CONV_TC_MODE");
+    g_ctx.conv_tc_mode = cmode && std::string(cmode) == "0" ? 0 : 1;
+    for (auto &s : P.steps)
+        if (s.kind == Step::CONV)
+            s.tc = s.conv && s.ctc_tap_off >= 0 && conv_path != "tiled" && conv_path != "direct" &&
+                   (conv_path == "tc" || s.C >= 4) &&
+                   conv_tc_shape_ok(s.KS, s.str_h, s.str_w, s.pad_h, s.pad_w, s.C, s.OC, s.pool, s.pk, s.pstr_h,
+                                    s.pstr_w, s.ppad_h, s.ppad_w, s.Ho, s.Wo);
     g_ctx.is_io_in.assign(P.buf_rows.size(), false);
     g_ctx.is_io_out.assign(P.buf_rows.size(), false);
     for (auto &io : P.inputs) g_ctx.is_io_in[(size_t)io.buf] = true;
@@ -535,6 +652,8 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, id);
         CUDA_TRY(configure_kernels());
         CUDA_TRY(mlp_tc_configure());
+        CUDA_TRY(conv_tc_configure());
+        CUDA_TRY(lstm2_tc_configure());
         CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
         CUDA_TRY(cudaMemcpy(d->arena, P.arena.data(), sizeof(float) * P.arena.size(), cudaMemcpyHostToDevice));
         CUDA_TRY(cudaMalloc(&d->err, 64 * sizeof(int)));
@@ -543,6 +662,28 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         std::memset(d->err_host, 0, 64 * sizeof(int));
         d->tc_args.assign(P.steps.size(), TcArgs{});
         d->lstm_args.assign(P.steps.size(), TcLstmArgs{});
+        d->lstm2_args.assign(P.steps.size(), TcLstm2Args{});
+        for (size_t si = 0; si + 1 < P.steps.size(); si++) {
+            const Step &s = P.steps[si];
+            if (s.kind != Step::LSTM || !s.fuse_next) continue;
+            const Step &s2 = P.steps[si + 1];
+            TcLstm2Args &a = d->lstm2_args[si];
+            a.arena = d->arena;
+            a.err = d->err;
+            a.T = s.T;
+            a.I = s.I;
+            const Step *ls[2] = {&s, &s2};
+            for (int k = 0; k < 2; k++) {
+                a.h0_const[k] = ls[k]->h0_const;
+                a.c0_const[k] = ls[k]->c0_const;
+                float *bias = k == 0 ? a.bias1 : a.bias2;
+                for (int c = 0; c < 256; c++) bias[c] = P.arena[(size_t)ls[k]->lstm_tc_b_off + (size_t)c];
+                const char *why = "";
+                if (!mlp_tc_encode_map(k == 0 ? &a.map1 : &a.map2, d->arena + ls[k]->lstm_tc_w_off, ls[k]->lstm_tc_Kp,
+                                       256, &why, 128))
+                    return Status::Err(ROSENNA_ERR_CUDA, why);
+            }
+        }
         for (size_t si = 0; si < P.steps.size(); si++) {
             const Step &s = P.steps[si];
             if (s.kind != Step::LSTM || !s.tc) continue;
@@ -815,7 +956,7 @@ int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *c
         for (size_t b = 0; b < ptr.size(); b++) ptr[b] = d->slots[0].scratch.empty() ? nullptr : d->slots[0].scratch[b];
         for (size_t i = 0; i < P.inputs.size(); i++) {
             if (!inputs[i]) return fail(ROSENNA_ERR_ARG, "null input pointer");
-            ptr[(size_t)P.inputs[i].buf] = const_cast<float *>(inputs[i]) + c0;
+            ptr[(size_t)P.inputs[i].buf] = const_cast<float *>(inputs[i]) + P.inputs[i].pre * c0;
             ld[(size_t)P.inputs[i].buf] = n;
         }
         for (size_t i = 0; i < P.outputs.size(); i++) {
@@ -910,19 +1051,28 @@ int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sam
             break;
         }
         case Step::LSTM:
-            name = s.tc ? "lstm_tc_kernel" : "lstm_ffma_kernel";
-            f = 2.0 * s.T * 4.0 * s.H * (double)(s.I + s.H);
+            if (s.fuse_next) {  // both layers
+                const Step &s2 = g_ctx.plan.steps[(size_t)i + 1];
+                name = "lstm2_tc_kernel";
+                f = 2.0 * s.T * 4.0 * s.H * (double)(s.I + s.H) + 2.0 * s2.T * 4.0 * s2.H * (double)(s2.I + s2.H);
+            } else if (i > 0 && g_ctx.plan.steps[(size_t)i - 1].fuse_next) {
+                name = "(in lstm2_tc_kernel)";
+            } else {
+                name = s.tc ? "lstm_tc_kernel" : "lstm_ffma_kernel";
+                f = 2.0 * s.T * 4.0 * s.H * (double)(s.I + s.H);
+            }
             break;
         case Step::CONV: {
             ConvArgs a{};
             a.conv = s.conv; a.relu = s.relu; a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.OC = s.OC; a.KS = s.KS;
             a.str_h = s.str_h; a.str_w = s.str_w; a.pool = s.pool; a.pk = s.pk;
-            name = conv_kernel_name(a);
+            name = s.tc ? "conv_tc_kernel" : conv_kernel_name(a);
             if (s.conv) f = 2.0 * s.Ho * s.Wo * s.OC * (double)s.C * s.KS * s.KS;
             break;
         }
         case Step::GATHER:
         case Step::COPY: name = "gather_kernel"; break;
+        case Step::DEINTERLEAVE: name = "deinterleave_kernel"; break;
         case Step::ACT:
         case Step::ADD: name = "act_kernel"; break;
     }
@@ -957,10 +1107,7 @@ extern "C" int rosenna_use_model_device_noalloc_f32(int64_t n, const float *cons
     if (n == 0) return ok();
 
     // intermediates of the plan, each rows x n floats, 256-byte aligned
-    std::vector<bool> used(P.buf_rows.size(), false);
-    for (auto &s : P.steps)
-        for (int b : {s.in, s.out, s.h0, s.c0, s.y, s.hn, s.cn})
-            if (b >= 0) used[(size_t)b] = true;
+    const std::vector<bool> used = used_buffers();
     std::vector<size_t> off(P.buf_rows.size(), 0);
     size_t need = 0;
     for (size_t b = 0; b < used.size(); b++) {

@@ -387,6 +387,34 @@ def infer_shapes(m: OnnxModel, constants: Dict[str, np.ndarray]) -> Dict[str, Li
                     for ax in axes:
                         o.insert(ax, 1)
                     outs = [o]
+            elif op == "Slice":
+                x = list(ins[0])
+                if len(nd.inputs) >= 3:  # opset >= 10: starts, ends[, axes[, steps]] as inputs
+                    st = [int(v) for v in np.asarray(value(nd.inputs[1])).reshape(-1)]
+                    en = [int(v) for v in np.asarray(value(nd.inputs[2])).reshape(-1)]
+                    ax = ([int(v) for v in np.asarray(value(nd.inputs[3])).reshape(-1)]
+                          if len(nd.inputs) > 3 and nd.inputs[3] else list(range(len(st))))
+                else:
+                    st, en = list(a["starts"]), list(a["ends"])
+                    ax = list(a.get("axes", range(len(st))))
+                for s_, e_, k in zip(st, en, ax):
+                    k = k + len(x) if k < 0 else k
+                    d = x[k]
+                    lo = max(0, min(d, s_ + d if s_ < 0 else s_))
+                    hi = max(lo, min(d, e_ + d if e_ < 0 else e_))
+                    x[k] = hi - lo
+                outs = [x]
+            elif op == "Gather":
+                x, idx = list(ins[0]), np.asarray(value(nd.inputs[1]))
+                k = int(a.get("axis", 0))
+                k = k + len(x) if k < 0 else k
+                outs = [x[:k] + list(idx.shape) + x[k + 1:]]
+            elif op == "Concat":
+                k = int(a["axis"])
+                x = list(ins[0])
+                k = k + len(x) if k < 0 else k
+                x[k] = sum(int(i[k]) for i in ins)
+                outs = [x]
             elif op == "LSTM":
                 x = ins[0]
                 hidden = int(a["hidden_size"])

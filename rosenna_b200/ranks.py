@@ -38,11 +38,13 @@ def shard_bounds(n: int, rank: int, world: int) -> Tuple[int, int]:
 
 
 def shard_rows(inputs_rows: Sequence[np.ndarray], rank: int, world: int) -> Tuple[int, int, List[np.ndarray]]:
-    """This rank's columns of every (rows, n) input, as contiguous arrays."""
+    """This rank's samples of every input, as contiguous arrays: columns of a
+    (rows, n) input, or axis 1 of a (post, n, pre) input (one whose batch is
+    not its first dimension, in the reference layout)."""
     n = int(inputs_rows[0].shape[1])
     for x in inputs_rows:
-        if x.ndim != 2 or x.shape[1] != n:
-            raise ValueError("inputs must be (rows, n) arrays over the same n samples")
+        if x.ndim not in (2, 3) or x.shape[1] != n:
+            raise ValueError("inputs must be (rows, n) or (post, n, pre) arrays over the same n samples")
     a, b = shard_bounds(n, rank, world)
     return a, b, [np.ascontiguousarray(x[:, a:b], dtype=np.float32) for x in inputs_rows]
 

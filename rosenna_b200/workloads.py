@@ -8,9 +8,11 @@ numpy.random.default_rng(2000 + k) (or a torch generator seeded the same way for
 device-side generation of large batches); values are generated in fp64 and
 rounded to fp32, and the same fp32 values feed the engine and the fp64 oracle.
 
-Inputs are returned in the batched reference layout as (rows, n) arrays: row r
-holds per-sample element r (Fortran order of the shape without its batch
-dimension) for all n samples.
+Inputs are returned in the batched reference layout: (rows, n) arrays, row r
+holding per-sample element r (Fortran order of the shape without its batch
+dimension) for all n samples, when the batch is the input's first dimension;
+the 2-layer LSTM's (2, N, 64) initial states, whose batch is the middle
+dimension, are (64, n, 2) C-order arrays (the Fortran order of (2, n, 64)).
 """
 from __future__ import annotations
 
@@ -139,13 +141,24 @@ def _cnn_inputs(n, rng):
     return [_f32(rng.standard_normal(size=(784, n)))]
 
 
-# ---- 5: two stacked LSTMs + MLP head -----------------------------------------------
+# ---- 5: a 2-layer stacked LSTM + MLP head ----------------------------------------
+class _StackedHead(nn.Module):
+    def __init__(self, lstm, head):
+        super().__init__()
+        self.lstm = lstm
+        self.head = nn.Sequential(*head)
+
+    def forward(self, x, h0, c0):
+        _, (hn, _) = self.lstm(x, (h0, c0))
+        return self.head(hn[-1])
+
+
 def _lstm2():
     torch.manual_seed(1005)
-    l1, l2 = nn.LSTM(12, 64, 1, batch_first=True), nn.LSTM(64, 64, 1, batch_first=True)
+    lstm = nn.LSTM(12, 64, 2, batch_first=True)
     head = [nn.Linear(64, 64), nn.ReLU(), nn.Linear(64, 3)]
-    g = writer.export_lstm([l1, l2], head, batch=1, seq_len=100, mode="hn_head", with_state=True)
-    return g, _LstmHead([l1, l2], head)
+    g = writer.export_stacked_lstm(lstm, head, batch=1, seq_len=100)
+    return g, _StackedHead(lstm, head)
 
 
 def _lstm2_inputs(n, rng):
@@ -157,8 +170,9 @@ def _lstm2_inputs(n, rng):
         x += (1.0 / k) * np.sin(2.0 * math.pi * k * t[:, None, None] / T + phi[None, :, :])
     x += 0.05 * rng.standard_normal(size=(T, F, n))
     rows = x.transpose(1, 0, 2).reshape(F * T, n)  # row f*T + t, i.e. t + T*f
-    h = [_f32(0.1 * rng.standard_normal(size=(64, n))) for _ in range(4)]  # h0, c0 of layer 0 then layer 1
-    return [_f32(rows), h[0], h[1], h[2], h[3]]
+    # h0, c0: (2, n, 64) in Fortran order = (64, n, 2) C order
+    h = [_f32(0.1 * rng.standard_normal(size=(64, n, 2))) for _ in range(2)]
+    return [_f32(rows), h[0], h[1]]
 
 
 WORKLOADS: Dict[str, Workload] = {
@@ -170,9 +184,9 @@ WORKLOADS: Dict[str, Workload] = {
                      4 * (400 + 4), [400], [4], _lstm, _lstm_inputs),
     "cnn": Workload(4, "cnn", "CNN 1x28x28: conv8+relu+max2, conv16+relu+avg2, 784-64-10, fp32", 65_536,
                     2 * 333_056, 4 * (784 + 10), [784], [10], _cnn, _cnn_inputs),
-    "lstm2": Workload(5, "lstm2", "2 stacked LSTMs I=12 H=64 T=100 + MLP 64-64-3, fp32", 1_048_576,
+    "lstm2": Workload(5, "lstm2", "LSTM I=12 H=64 2 layers T=100 + MLP 64-64-3, fp32", 1_048_576,
                       2 * (100 * 256 * 76 + 100 * 256 * 128 + 64 * 64 + 64 * 3), 4 * (1200 + 4 * 64 + 3),
-                      [1200, 64, 64, 64, 64], [3], _lstm2, _lstm2_inputs),
+                      [1200, 128, 128], [3], _lstm2, _lstm2_inputs),
 }
 
 
@@ -206,8 +220,9 @@ def torch_reference(name: str, module, inputs: List[np.ndarray]) -> List[np.ndar
         x = torch.from_numpy(x).permute(2, 1, 0).contiguous()  # (n, T, I)
         if name == "lstm":
             y = m(x)
-        else:
-            st = [torch.from_numpy(a.astype(np.float64).T.copy()).unsqueeze(0) for a in inputs[1:]]
+        else:  # (64, n, 2) C order -> (2, n, 64)
+            st = [torch.from_numpy(np.asarray(a, dtype=np.float64).reshape(64, n, 2).transpose(2, 1, 0).copy())
+                  for a in inputs[1:]]
             y = m(x, *st)
         return [y.numpy().T.copy()]
 
@@ -235,5 +250,5 @@ def make_inputs_torch(name: str, n: int, device="cuda", seed_offset: int = 0) ->
         phi = torch.rand((F, 1, n), **f64) * (2.0 * math.pi)
         x += (1.0 / k) * torch.sin(2.0 * math.pi * k * t / T + phi)
     x += 0.05 * torch.randn((F, T, n), **f64)
-    states = [(0.1 * torch.randn((64, n), **f64)).float() for _ in range(4)]
+    states = [(0.1 * torch.randn((64, n, 2), **f64)).float() for _ in range(2)]  # (2, n, 64) Fortran order
     return [x.reshape(F * T, n).float()] + states

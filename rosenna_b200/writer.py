@@ -248,6 +248,34 @@ def write_model_files(g: Graph, out_dir: str) -> None:
             inputs.append(["output" + extra, 2])
             io_map[node.outputs[0]] = "output" + extra
             extra = str(int(extra) + 1)
+        elif layer in ("Slice", "Gather", "Concat"):
+            # modelParserONNX.py:519-523 passes these through unwritten; a stacked
+            # LSTM export needs them (per-layer slices of its (L, N, H) initial
+            # states, h_n = Concat of the layers' h_n, the head on h_n[-1]).  They
+            # are written as architecture entries only (no weights):
+            #   ('Slice', [x], [out], [axes, starts, ends])
+            #   ('Gather', [x], [out], [axis, index])
+            #   ('Concat', [x0, x1, ..], [out], [axis])
+            src = node.inputs[0]
+            if layer == "Slice":
+                if len(node.inputs) >= 3:  # opset >= 10: starts, ends, axes as constant inputs
+                    starts = [int(v) for v in np.asarray(find_weights(node.inputs[1])).reshape(-1)]
+                    ends = [int(v) for v in np.asarray(find_weights(node.inputs[2])).reshape(-1)]
+                    axes = ([int(v) for v in np.asarray(find_weights(node.inputs[3])).reshape(-1)]
+                            if len(node.inputs) > 3 and node.inputs[3] else list(range(len(starts))))
+                else:
+                    starts, ends = list(node.attrs["starts"]), list(node.attrs["ends"])
+                    axes = list(node.attrs.get("axes", range(len(starts))))
+                ends = [min(e, 2 ** 31 - 1) for e in ends]
+                arch.append(("Slice", [io_map[src]], ["output" + extra], [axes, starts, ends]))
+            elif layer == "Gather":
+                index = int(np.asarray(find_weights(node.inputs[1])).reshape(-1)[0])
+                arch.append(("Gather", [io_map[src]], ["output" + extra], [int(node.attrs.get("axis", 0)), index]))
+            else:
+                arch.append(("Concat", [io_map[x] for x in node.inputs], ["output" + extra], [int(node.attrs["axis"])]))
+            inputs.append(["output" + extra, len(inter[node.outputs[0]])])
+            io_map[node.outputs[0]] = "output" + extra
+            extra = str(int(extra) + 1)
         elif layer == "Conv":  # :333-390
             f_lines.append(layer)
             attributes = dict(node.attrs)
@@ -535,3 +563,48 @@ def export_lstm(lstms: Sequence, head: Sequence, batch: int, seq_len: int, mode:
     b.vi["output"] = b.vi.pop(out_name, out_shape)
     return Graph(nodes=b.nodes, inputs=g_inputs, outputs=[("output", out_shape)], initializers=b.inits,
                  value_info=b.vi, constants=b.consts, true_weights=b.true_weights)
+
+
+def export_stacked_lstm(lstm, head: Sequence, batch: int, seq_len: int) -> Graph:
+    """Graph of one batch-first nn.LSTM with num_layers >= 2, given (h0, c0) of
+    shape (num_layers, N, H), with a head on the last layer's h_n (hn[-1]), as
+    torch.onnx.export emits it (opset 10): the input Transpose; per layer a
+    Slice of h0 and c0 along axis 0, the LSTM node, and a Squeeze of its output
+    sequence as the next layer's input; h_n = Concat of the layers' h_n along
+    axis 0; Gather(h_n, -1, axis 0) into the head."""
+    b = _Builder()
+    L, H, I = lstm.num_layers, lstm.hidden_size, lstm.input_size
+    if L < 2 or not lstm.batch_first or lstm.bidirectional:
+        raise TypeError("export_stacked_lstm takes a batch-first, one-direction nn.LSTM with num_layers >= 2")
+    g_inputs = [("input", [batch, seq_len, I]), ("hidden_state", [L, batch, H]), ("cell_state", [L, batch, H])]
+    (x,) = b.add("Transpose", ["input"], [[seq_len, batch, I]], {"perm": [1, 0, 2]})
+    hns = []
+    for k in range(L):
+        starts, ends, axes = (b.const(np.asarray([v], dtype=np.int64)) for v in (k, k + 1, 0))
+        (h_k,) = b.add("Slice", ["hidden_state", starts, ends, axes], [[1, batch, H]])
+        starts, ends, axes = (b.const(np.asarray([v], dtype=np.int64)) for v in (k, k + 1, 0))
+        (c_k,) = b.add("Slice", ["cell_state", starts, ends, axes], [[1, batch, H]])
+        w_ih, w_hh = _np32(getattr(lstm, f"weight_ih_l{k}")), _np32(getattr(lstm, f"weight_hh_l{k}"))
+        b_ih, b_hh = _np32(getattr(lstm, f"bias_ih_l{k}")), _np32(getattr(lstm, f"bias_hh_l{k}"))
+        W = b.weight(w_ih, folded=w_ih.reshape(1, 4 * H, -1))
+        R = b.weight(w_hh, folded=w_hh.reshape(1, 4 * H, H))
+        B = b.name("w")
+        b.inits[B] = np.concatenate([b_ih, b_hh]).reshape(1, 8 * H)
+        b.true_weights += [b_ih, b_hh]
+        y, yh, _ = b.add("LSTM", [x, W, R, B, "", h_k, c_k], [[seq_len, 1, batch, H], [1, batch, H], [1, batch, H]],
+                         {"hidden_size": H})
+        hns.append(yh)
+        if k + 1 < L:
+            (x,) = b.add("Squeeze", [y], [[seq_len, batch, H]], {"axes": [1]})
+    (hn,) = b.add("Concat", hns, [[L, batch, H]], {"axis": 0})
+    idx = b.const(np.asarray(-1, dtype=np.int64))
+    (last,) = b.add("Gather", [hn, idx], [[batch, H]], {"axis": 0})
+    out, shp = last, [batch, H]
+    for m in head:
+        out, shp = _emit_module(b, m, out, shp)
+    for n in b.nodes:
+        n.outputs = ["output" if o == out else o for o in n.outputs]
+        n.inputs = ["output" if i == out else i for i in n.inputs]
+    b.vi["output"] = b.vi.pop(out, shp)
+    return Graph(nodes=b.nodes, inputs=g_inputs, outputs=[("output", shp)], initializers=b.inits, value_info=b.vi,
+                 constants=b.consts, true_weights=b.true_weights)

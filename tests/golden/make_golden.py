@@ -110,6 +110,26 @@ def lstm_case(name, seed, I, H, T, head_fn, mode, batch=1):
     _write_case(name, g, [x.numpy(), h0.numpy(), c0.numpy()], y.numpy())
 
 
+def stacked_lstm_case(name, seed, I, H, T, layers, head_fn, batch=1):
+    """A batch-first nn.LSTM with num_layers >= 2, given (h0, c0) of shape
+    (layers, N, H), with a head on the last layer's h_n: the graph
+    torch.onnx.export gives it (Slice of the states per layer, Concat of h_n,
+    Gather of the last layer), which the reference parser passes through
+    unwritten (modelParserONNX.py:519-523) and this build's front end writes."""
+    torch.manual_seed(seed)
+    lstm = nn.LSTM(I, H, layers, batch_first=True)
+    head = head_fn()
+    x = torch.ones(batch, T, I)
+    h0 = torch.ones(layers, batch, H) * 0.5
+    c0 = torch.ones(layers, batch, H) * -0.25
+    g = writer.export_stacked_lstm(lstm, head, batch, T)
+    net = nn.Sequential(*head).double()
+    with torch.no_grad():
+        _, (hn, _) = lstm.double()(x.double(), (h0.double(), c0.double()))
+        y = net(hn[-1])
+    _write_case(name, g, [x.numpy(), h0.numpy(), c0.numpy()], y.numpy())
+
+
 def conv_case(name, seed, mods_fn, shape):
     torch.manual_seed(seed)
     mods = mods_fn()
@@ -245,6 +265,8 @@ def main():
     lstm_case("lstm_output", 106, 10, 20, 25, None, "y")
     lstm_case("lstm_gemm", 107, 5, 2, 2, _head, "y_head")
     lstm_case("lstm_gemm_hid", 108, 5, 2, 2, _head, "hn_head")
+    # a stacked nn.LSTM(num_layers=2) exported as one graph (Slice / Concat / Gather)
+    stacked_lstm_case("lstm_stacked", 120, 5, 6, 4, 2, lambda: [nn.Linear(6, 3), nn.Tanh()])
     # Convolutions and pooling: goldenFiles/conv_*, maxpool_*, avgpool_basic
     conv_case("conv_basic", 109, lambda: [nn.Conv2d(2, 3, 3)], (2, 2, 7, 7))
     conv_case("conv_padding", 110, lambda: [nn.Conv2d(2, 3, 3, padding=[2, 3])], (1, 2, 6, 6))

@@ -60,7 +60,7 @@ def test_c_solver_matches_oracle(case, tmp_path):
     got = np.array([float(v) for v in lines[1].split()])
     m = OracleModel(goldens.case_dir(case))
     rows = [int(np.prod(s)) for s in m.input_shapes]
-    ref = m.run_batched(1, [np.ones(k) for k in rows], [1] * len(rows), [1])[0]
+    ref = m.run_batched(1, [np.ones(k) for k in rows])[0]
     res = parity.compare(got, ref)
     print(f"{case}: {parity.describe(res)}")
     assert res["ok"], parity.describe(res)

@@ -36,7 +36,7 @@ def test_plan_fuses_the_workloads(tmp_path):
         "wide_mlp": ["mlp b0->b1 [16x256:relu 256x256:relu 256x256:relu 256x256:relu 256x256:relu 256x8]"],
         "lstm": ["lstm b0 T=50 I=8 H=32", "mlp"],
         "cnn": ["conv", "relu maxpool k=2 s=2 -> 14x14", "relu avgpool k=2 s=2 -> 7x7", "mlp"],
-        "lstm2": ["lstm b0 T=100 I=12 H=64", "lstm b5 T=100 I=64 H=64", "mlp"],
+        "lstm2": ["deinterleave", "lstm b0 T=100 I=12 H=64", "T=100 I=64 H=64", "mlp"],
     }
     for name, parts in expect.items():
         d = tmp_path / name
@@ -126,7 +126,7 @@ def test_oracle_matches_torch_on_workloads(name, tmp_path):
     mod = workloads.write_model(name, str(tmp_path))
     n = 5
     ins = workloads.make_inputs(name, n)
-    out = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+    out = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
     ref = workloads.torch_reference(name, mod, ins)[0]
     np.testing.assert_allclose(out.reshape(ref.shape), ref, rtol=0, atol=1e-12)
 

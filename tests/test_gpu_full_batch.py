@@ -34,7 +34,7 @@ def oracle_subset(model_dir, ins, idx):
     """The oracle on the samples `idx` of device inputs `ins` ((rows, n) each)."""
     t = torch.from_numpy(idx).to(ins[0].device)
     sub = [x.index_select(1, t).double().cpu().numpy() for x in ins]
-    return OracleModel(model_dir).run_batched(len(idx), sub, [1] * len(sub), [1])[0].reshape(-1, len(idx))
+    return OracleModel(model_dir).run_batched(len(idx), sub)[0].reshape(-1, len(idx))
 
 
 @pytest.mark.parametrize("name", list(workloads.WORKLOADS))

@@ -70,5 +70,39 @@ def test_ffma_lstm_shapes(case, tmp_path, monkeypatch):
         ins = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) if i == 0
                else rng.uniform(-0.5, 0.5, size=(r, n)).astype(np.float32) for i, r in enumerate(rows)]
         out = api.use_model_rows(ins)[0]
-        ref = oracle.run_batched(n, ins, [1] * len(ins), [1])[0]
+        ref = oracle.run_batched(n, ins)[0]
+        assert_close(out, ref.reshape(out.shape), f"{case} n={n}")
+
+
+# the fused two-layer tensor-core kernel: hidden size 64 in both layers,
+# layer-1 input width <= 32
+FUSED = {
+    "x2_i12_t7_hn": (12, 7, "hn_head", True),
+    "x2_i1_t3_y": (1, 3, "y", True),
+    "x2_i32_t2_cn": (32, 2, "cn", True),
+    "x2_i5_t1_hn": (5, 1, "hn_head", False),
+    "x2_i20_t9_y": (20, 9, "y", False),
+}
+
+
+@pytest.mark.parametrize("case", sorted(FUSED))
+def test_fused_two_layer_lstm_shapes(case, tmp_path):
+    I, T, mode, state = FUSED[case]
+    torch.manual_seed(len(case) * 7 + I)
+    lstms = [nn.LSTM(I, 64, 1, batch_first=True), nn.LSTM(64, 64, 1, batch_first=True)]
+    head = [nn.Linear(64, 3), nn.Tanh()] if mode == "hn_head" else []
+    g = writer.export_lstm(lstms, head, batch=1, seq_len=T, mode=mode, with_state=state)
+    d = str(tmp_path)
+    writer.write_model_files(g, d)
+    api.initialize(d)
+    plan = api.plan_description()
+    assert "lstm2_tc" in plan, plan
+    oracle = OracleModel(d)
+    rows = [int(np.prod(s)) // s[b] for s, b in api.input_specs()]
+    rng = np.random.default_rng(len(case))
+    for n in (1, 129, 1000, 4097):
+        ins = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) if i == 0
+               else rng.uniform(-0.5, 0.5, size=(r, n)).astype(np.float32) for i, r in enumerate(rows)]
+        out = api.use_model_rows(ins)[0]
+        ref = oracle.run_batched(n, ins)[0]
         assert_close(out, ref.reshape(out.shape), f"{case} n={n}")

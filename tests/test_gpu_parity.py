@@ -78,7 +78,7 @@ def test_golden_case_batched(case, n):
     rows = [int(np.prod(s)) // s[b] for s, b in api.input_specs()]
     ins = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) for r in rows]
     out = api.use_model_rows(ins)[0]
-    ref = OracleModel(d).run_batched(n, ins, [1] * len(ins), [1])[0]
+    ref = OracleModel(d).run_batched(n, ins)[0]
     assert_close(out, ref.reshape(out.shape), f"{case} n={n}")
 
 
@@ -98,7 +98,7 @@ def test_workload_parity(name, n, tmp_path):
     api.initialize(str(tmp_path))
     ins = workloads.make_inputs(name, n, seed_offset=n)
     out = api.use_model_rows(ins)[0]
-    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
     assert_close(out, ref.reshape(out.shape), f"{name} n={n}")
 
 
@@ -123,7 +123,7 @@ def test_large_batch_small_mlp_chunks_and_tails(tmp_path):
     n = (1 << 20) + 333
     ins = workloads.make_inputs("small_mlp", n, seed_offset=3)
     out = api.use_model_rows(ins)[0]
-    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
     assert_close(out, ref.reshape(out.shape), "small_mlp large")
 
 
@@ -150,7 +150,7 @@ def test_multi_gpu_split_matches(name, tmp_path):
     n = 10007
     ins = workloads.make_inputs(name, n, seed_offset=5)
     out = api.use_model_rows(ins)[0]
-    ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+    ref = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
     assert_close(out, ref.reshape(out.shape), f"{name} multi-gpu")
 
 
@@ -169,23 +169,26 @@ def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
     for n in (129, 4099):
         ins = workloads.make_inputs(name, n, seed_offset=7 + n)
         out = api.use_model_rows(ins)[0]
-        ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+        ref = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
         assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
 
 
-@pytest.mark.parametrize("path", ["tc", "ffma"])
+@pytest.mark.parametrize("path", ["tc", "tc_unfused", "ffma"])
 @pytest.mark.parametrize("name", ["lstm", "lstm2"])
 def test_lstm_kernel_paths(name, path, tmp_path, monkeypatch):
-    """Both LSTM kernels (tcgen05 3xTF32 and FFMA) on both LSTM workloads."""
-    monkeypatch.setenv("ROSENNA_LSTM_PATH", path)
+    """The LSTM kernels (tcgen05 3xTF32 per layer, the fused two-layer tcgen05
+    kernel, FFMA) on both LSTM workloads."""
+    monkeypatch.setenv("ROSENNA_LSTM_PATH", "ffma" if path == "ffma" else "tc")
+    monkeypatch.setenv("ROSENNA_LSTM2_FUSE", "0" if path == "tc_unfused" else "1")
     workloads.write_model(name, str(tmp_path))
     api.initialize(str(tmp_path))
     desc = api.plan_description()
-    assert ("lstm_tc" in desc) == (path == "tc"), desc
+    assert ("lstm_tc" in desc) == (path != "ffma"), desc
+    assert ("lstm2_tc" in desc) == (name == "lstm2" and path == "tc"), desc
     for n in (1, 129, 1000, 4099):
         ins = workloads.make_inputs(name, n, seed_offset=3 + n)
         out = api.use_model_rows(ins)[0]
-        ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1] * len(ins), [1])[0]
+        ref = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
         assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
 
 
@@ -207,7 +210,7 @@ def test_cnn_conv_paths(conv_path, tmp_path):
         for n in (1, 37, 1000):
             ins = workloads.make_inputs('cnn', n, seed_offset=11 + n)
             out = api.use_model_rows(ins)[0]
-            ref = OracleModel({repr(str(tmp_path))}).run_batched(n, ins, [1], [1])[0]
+            ref = OracleModel({repr(str(tmp_path))}).run_batched(n, ins)[0]
             assert_close(out, ref.reshape(out.shape), f'cnn {conv_path} n={{n}}')
         d = goldens.case_dir('cnn_small')
         api.initialize(d)
@@ -236,7 +239,7 @@ def test_golden_mlps_on_tensor_cores(case, tail, monkeypatch):
     rows = [int(np.prod(s)) // s[b] for s, b in api.input_specs()]
     xs = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) for r in rows]
     out = api.use_model_rows(xs)[0]
-    ref = OracleModel(d).run_batched(n, xs, [1] * len(xs), [1])[0]
+    ref = OracleModel(d).run_batched(n, xs)[0]
     assert_close(out, ref.reshape(out.shape), f"{case} tc n={n}")
 
 
@@ -260,5 +263,5 @@ def test_conv_kernel_shapes(ks, pool, pk, tmp_path):
     for n in (1, 45, 1000):
         ins = [np.random.default_rng(n).uniform(-1, 1, size=(3 * 11 * 11, n)).astype(np.float32)]
         out = api.use_model_rows(ins)[0]
-        ref = OracleModel(str(tmp_path)).run_batched(n, ins, [1], [1])[0]
+        ref = OracleModel(str(tmp_path)).run_batched(n, ins)[0]
         assert_close(out, ref.reshape(out.shape), f"k={ks} {pool}{pk} n={n}")

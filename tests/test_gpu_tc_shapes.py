@@ -77,5 +77,5 @@ def test_tc_chain_shapes(case, tail, dual, tmp_path, monkeypatch):
     for n in (1, 129, 1000, 4097) + ((50001,) if narrow(case) and dual == "1" else ()):
         x = rng.uniform(-1.5, 1.5, size=(widths[0], n)).astype(np.float32)
         out = api.use_model_rows([x])[0]
-        ref = oracle.run_batched(n, [x], [1], [1])[0]
+        ref = oracle.run_batched(n, [x])[0]
         assert_close(out, ref.reshape(out.shape), f"{case} tail={tail} dual={dual} n={n}")

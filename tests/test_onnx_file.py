@@ -114,11 +114,13 @@ def _graphs():
     torch.manual_seed(6)
     cnn_flatten = writer.export_sequential([nn.Conv2d(1, 4, 3, padding=1), nn.ReLU(), nn.MaxPool2d(2, 2),
                                             nn.Flatten(), nn.Linear(64, 3)], [1, 1, 8, 8])
-    return {"mlp": mlp, "cnn": cnn, "lstm": lstm, "cnn_flatten": cnn_flatten}
+    torch.manual_seed(7)
+    stacked = writer.export_stacked_lstm(nn.LSTM(3, 4, 2, batch_first=True), [nn.Linear(4, 2)], 1, 5)
+    return {"mlp": mlp, "cnn": cnn, "lstm": lstm, "cnn_flatten": cnn_flatten, "stacked_lstm": stacked}
 
 
 @pytest.mark.parametrize("raw", [True, False])
-@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm", "cnn_flatten"])
+@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm", "cnn_flatten", "stacked_lstm"])
 def test_decoded_graph_writes_the_same_files(name, raw, tmp_path):
     g = _graphs()[name]
     (tmp_path / "m.onnx").write_bytes(encode(g, raw=raw))
@@ -133,7 +135,7 @@ def test_decoded_graph_writes_the_same_files(name, raw, tmp_path):
     assert _files(tmp_path / "direct") == _files(tmp_path / "decoded")
 
 
-@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm", "cnn_flatten"])
+@pytest.mark.parametrize("name", ["mlp", "cnn", "lstm", "cnn_flatten", "stacked_lstm"])
 def test_shape_inference_recovers_value_info(name, tmp_path):
     g = _graphs()[name]
     (tmp_path / "m.onnx").write_bytes(encode(g, with_value_info=False))

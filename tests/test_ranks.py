@@ -55,7 +55,7 @@ def oracle_runner(model_dir, dtype=np.float32, threads=1):
     m = OracleModel(model_dir)
 
     def run(xs, k):
-        outs = m.run_batched(k, xs, [1] * len(xs), [1] * len(m.output_shapes), threads)
+        outs = m.run_batched(k, xs, threads=threads)
         return [o.reshape(int(np.prod(s)), k).astype(dtype) for o, s in zip(outs, m.output_shapes)]
 
     return run
