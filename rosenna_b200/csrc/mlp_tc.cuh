@@ -105,6 +105,12 @@ cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
 // the driver entry point or encode fails.
 bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, const char **why, int box_rows = 0);
 
+// One LSTM layer with I <= 32, H <= 32 (4H <= 128), each column group running
+// a tile of its own (lstm_dual_tc.cu); TcLstmArgs as for launch_lstm_tc.
+bool lstm_dual_tc_regs_ok();
+cudaError_t lstm_dual_tc_configure();
+cudaError_t launch_lstm_dual_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
+
 // The fused two-layer LSTM kernel.
 bool lstm2_tc_regs_ok();
 cudaError_t lstm2_tc_configure();

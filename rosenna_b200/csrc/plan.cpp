@@ -616,12 +616,9 @@ Status Builder::op_conv(const PyVal &e) {  // modelCreator.fpp:103-105, layers.f
     s.w_off = put(w.data(), w.size());
     s.b_off = put(b.data(), b.size());
     if (s.KS == 3 && s.str_h == 1 && s.str_w == 1 && s.C <= 8 && s.OC <= 16) {
-        std::vector<float> img((size_t)kConvTcBFloatsTap);
-        conv_tc_pack(w.data(), s.OC, s.C, 0, img.data());
-        s.ctc_tap_off = put(img.data(), img.size());
-        img.assign((size_t)kConvTcBFloats, 0.f);
-        conv_tc_pack(w.data(), s.OC, s.C, 1, img.data());
-        s.ctc_win_off = put(img.data(), img.size());
+        std::vector<float> img((size_t)kConvTcBFloats);
+        conv_tc_pack(w.data(), s.OC, s.C, img.data());
+        s.ctc_off = put(img.data(), img.size());
     }
     s.in = x.buf;
     s.out = new_buf((int64_t)s.OC * s.Ho * s.Wo);
@@ -1126,7 +1123,7 @@ std::string Plan::describe() const {
                 o << "]\n";
                 break;
             case Step::LSTM:
-                o << (s.tc ? "lstm_tc b" : "lstm b") << s.in << " T=" << s.T << " I=" << s.I << " H=" << s.H << " h0=b" << s.h0 << " c0=b"
+                o << (s.tc ? (s.lstm_dual ? "lstm_tc_dual b" : "lstm_tc b") : "lstm b") << s.in << " T=" << s.T << " I=" << s.I << " H=" << s.H << " h0=b" << s.h0 << " c0=b"
                   << s.c0 << " -> y=b" << s.y << " hn=b" << s.hn << " cn=b" << s.cn << "\n";
                 break;
             case Step::CONV:

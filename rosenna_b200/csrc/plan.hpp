@@ -51,15 +51,17 @@ struct Step {
     // this LSTM step and the next one (which reads only its y) run as one fused
     // two-layer kernel; its y is never materialised (decided at initialize)
     bool fuse_next = false;
+    // run on the dual-tile tensor-core kernel (I <= 32, H <= 32; decided at initialize)
+    bool lstm_dual = false;
 
     // CONV (+ReLU) (+pool); conv == false means pooling only
     bool conv = true, relu = false;
     int C = 0, Hin = 0, Win = 0, OC = 0, KS = 0, pad_h = 0, pad_w = 0, str_h = 1, str_w = 1, Ho = 0, Wo = 0;
     int pool = 0, pk = 1, ppad_h = 0, ppad_w = 0, pstr_h = 1, pstr_w = 1, Hq = 0, Wq = 0;  // pool: 0 none, 1 max, 2 avg
     int64_t so_c = 1, so_h = 0, so_w = 0;  // output row = oc*so_c + h*so_h + w*so_w
-    // tensor-core (implicit GEMM) B images of a 3x3 stride-1 conv with C <= 8
-    // and OC <= 16, per tap and per window (conv_tc.cuh); -1 when not packed
-    int64_t ctc_tap_off = -1, ctc_win_off = -1;
+    // tensor-core (implicit GEMM) B image of a 3x3 stride-1 conv with C <= 8
+    // and OC <= 16 (conv_tc.cuh); -1 when not packed
+    int64_t ctc_off = -1;
 
     // packed weights (MLP: per layer; LSTM/CONV: here)
     int64_t w_off = -1, b_off = -1;

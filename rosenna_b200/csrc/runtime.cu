@@ -75,7 +75,6 @@ struct Context {
     std::vector<int64_t> mlp_table_off;        // per step: index into mlp_tables, device offset in arena
     std::vector<int64_t> mlp_table_arena_off;
     std::vector<bool> is_io_in, is_io_out;
-    int conv_tc_mode = 1;  // tensor-core conv MMA form: 0 per tap (N = 16), 1 per window (N = 64)
 };
 
 Context g_ctx;
@@ -287,7 +286,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                     if (s.hn >= 0) { a.hn = ptr[(size_t)s.hn]; a.ld_hn = ld[(size_t)s.hn]; }
                     if (s.cn >= 0) { a.cn = ptr[(size_t)s.cn]; a.ld_cn = ld[(size_t)s.cn]; }
                     a.n = cnt;
-                    e = launch_lstm_tc(a, d.num_sms, stream);
+                    e = s.lstm_dual ? launch_lstm_dual_tc(a, d.num_sms, stream) : launch_lstm_tc(a, d.num_sms, stream);
                     launches++;
                     if (e == cudaSuccess)
                         e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
@@ -320,7 +319,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 if (s.tc) {
                     ConvTcArgs a{};
                     a.arena = arena;
-                    a.bt_off = g_ctx.conv_tc_mode == 0 ? s.ctc_tap_off : s.ctc_win_off;
+                    a.bt_off = s.ctc_off;
                     a.b_off = s.b_off;
                     a.in = ptr[(size_t)s.in];
                     a.ld_in = ld[(size_t)s.in];
@@ -331,7 +330,8 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                     a.err = d.err;
                     a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.pad = s.pad_h; a.OC = s.OC;
                     a.Hq = s.Hq; a.Wq = s.Wq; a.pool = s.pool; a.relu = s.relu ? 1 : 0;
-                    a.mode = g_ctx.conv_tc_mode;
+                    const ConvTcGeom geo = conv_tc_geometry(s.C, s.OC);
+                    a.cp = geo.cp; a.bwin = geo.bwin; a.nch = geo.nch;
                     e = launch_conv_tc(a, d.num_sms, stream);
                     launches++;
                     if (e == cudaSuccess)
@@ -577,14 +577,22 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         }
         s.tc = tc_ok && eligible && mlp_path != "ffma" && (mlp_path == "tc" || widest >= 64);
     }
-    // tensor-core LSTM for 128 < 4H <= 256, both column halves busy (with 4H <= 128
-    // one half idles and the per-step chain is latency-bound: the FFMA kernel is
-    // faster); ROSENNA_LSTM_PATH=ffma / =tc force either kernel
+    // tensor-core LSTM: for 128 < 4H <= 256 the kernel whose two column groups
+    // split one tile's gates; for I <= 32 and H <= 32 the dual-tile kernel (each
+    // group a tile of its own, all 4H gates in one N = 4H MMA), else the FFMA
+    // kernel.  ROSENNA_LSTM_PATH=ffma / =tc (the split kernel wherever it fits) /
+    // =dual force a kernel
     const char *lpath = getenv("ROSENNA_LSTM_PATH");
     const std::string lstm_path = lpath ? lpath : "";
+    const bool dual_ok = tc_ok && lstm_dual_tc_regs_ok();
     for (auto &s : P.steps)
-        if (s.kind == Step::LSTM)
-            s.tc = tc_ok && lstm_path != "ffma" && s.lstm_tc_w_off >= 0 && (lstm_path == "tc" || 4 * s.H > 128);
+        if (s.kind == Step::LSTM) {
+            const bool dual_fits = s.lstm_tc_w_off >= 0 && s.I <= 32 && s.H <= 32 && s.lstm_tc_nx == 1 &&
+                                   s.lstm_tc_nh == 1 && s.lstm_tc_Np <= 128;
+            s.lstm_dual = dual_ok && dual_fits && lstm_path != "ffma" && lstm_path != "tc";
+            s.tc = tc_ok && lstm_path != "ffma" && s.lstm_tc_w_off >= 0 &&
+                   (lstm_path == "tc" || 4 * s.H > 128 || s.lstm_dual);
+        }
     // two stacked LSTM layers with H = 64 (and a layer-1 input of at most 32)
     // run as one fused kernel when the second layer is the only reader of the
     // first layer's output sequence; ROSENNA_LSTM2_FUSE=0 keeps them apart
@@ -609,22 +617,17 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         if (!other_reader) a.fuse_next = true;
     }
     // tensor-core conv (implicit GEMM) for the 3x3 stride-1 conv + 2x2 pool shapes
-    // it covers, with at least 4 input channels (a K-step holds 8 channels: fewer
-    // would multiply mostly zero padding; such convs stay on the CUDA cores);
+    // it covers, with one input channel (K-steps of 8 patch positions) or at
+    // least 4 (K-steps of a position's 8 channels: with 2 or 3 the zero padding
+    // outweighs the tensor cores and the CUDA-core kernel is faster);
     // ROSENNA_CONV_PATH=tiled|direct keeps the CUDA-core kernels, =tc takes the
-    // tensor cores for every shape they cover; ROSENNA_CONV_TC_MODE=0|1 picks
-    // the MMA form
+    // tensor cores for every shape they cover
     const char *cpath = getenv("ROSENNA_CONV_PATH");
     const std::string conv_path = cpath ? cpath : "";
-    // (an M = 128 tcgen05 MMA of N <= 128 columns takes ~65 cycles whatever N,
-    // measured: the per-window form's 48 MMAs of N = 64 cost less than the
-    // per-tap form's 108 of N = 16)
-    const char *cmode = getenv("ROSENNA_CONV_TC_MODE");
-    g_ctx.conv_tc_mode = cmode && std::string(cmode) == "0" ? 0 : 1;
     for (auto &s : P.steps)
         if (s.kind == Step::CONV)
-            s.tc = s.conv && s.ctc_tap_off >= 0 && conv_path != "tiled" && conv_path != "direct" &&
-                   (conv_path == "tc" || s.C >= 4) &&
+            s.tc = tc_ok && s.conv && s.ctc_off >= 0 && conv_path != "tiled" && conv_path != "direct" &&
+                   (conv_path == "tc" || s.C == 1 || s.C >= 4) &&
                    conv_tc_shape_ok(s.KS, s.str_h, s.str_w, s.pad_h, s.pad_w, s.C, s.OC, s.pool, s.pk, s.pstr_h,
                                     s.pstr_w, s.ppad_h, s.ppad_w, s.Ho, s.Wo);
     g_ctx.is_io_in.assign(P.buf_rows.size(), false);
@@ -654,6 +657,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         CUDA_TRY(mlp_tc_configure());
         CUDA_TRY(conv_tc_configure());
         CUDA_TRY(lstm2_tc_configure());
+        CUDA_TRY(lstm_dual_tc_configure());
         CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
         CUDA_TRY(cudaMemcpy(d->arena, P.arena.data(), sizeof(float) * P.arena.size(), cudaMemcpyHostToDevice));
         CUDA_TRY(cudaMalloc(&d->err, 64 * sizeof(int)));
@@ -1058,7 +1062,7 @@ int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sam
             } else if (i > 0 && g_ctx.plan.steps[(size_t)i - 1].fuse_next) {
                 name = "(in lstm2_tc_kernel)";
             } else {
-                name = s.tc ? "lstm_tc_kernel" : "lstm_ffma_kernel";
+                name = s.tc ? (s.lstm_dual ? "lstm_dual_tc_kernel" : "lstm_tc_kernel") : "lstm_ffma_kernel";
                 f = 2.0 * s.T * 4.0 * s.H * (double)(s.I + s.H);
             }
             break;

@@ -74,6 +74,27 @@ def test_ffma_lstm_shapes(case, tmp_path, monkeypatch):
         assert_close(out, ref.reshape(out.shape), f"{case} n={n}")
 
 
+@pytest.mark.parametrize("case", sorted(c for c, v in CASES.items() if v[0] <= 32 and max(v[1]) <= 32))
+def test_dual_tile_lstm_shapes(case, tmp_path, monkeypatch):
+    """The dual-tile tensor-core kernel (I <= 32, H <= 32: each column group a
+    tile of its own), the default for these shapes."""
+    monkeypatch.delenv("ROSENNA_LSTM_PATH", raising=False)
+    d = str(tmp_path)
+    build(case, d)
+    api.initialize(d)
+    plan = api.plan_description()
+    assert "lstm_tc_dual" in plan, plan
+    oracle = OracleModel(d)
+    rows = [int(np.prod(s)) // s[b] for s, b in api.input_specs()]
+    rng = np.random.default_rng(len(case) + 1)
+    for n in (1, 129, 1000, 4097):
+        ins = [rng.uniform(-1.5, 1.5, size=(r, n)).astype(np.float32) if i == 0
+               else rng.uniform(-0.5, 0.5, size=(r, n)).astype(np.float32) for i, r in enumerate(rows)]
+        out = api.use_model_rows(ins)[0]
+        ref = oracle.run_batched(n, ins)[0]
+        assert_close(out, ref.reshape(out.shape), f"{case} n={n}")
+
+
 # the fused two-layer tensor-core kernel: hidden size 64 in both layers,
 # layer-1 input width <= 32
 FUSED = {

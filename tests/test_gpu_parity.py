@@ -173,18 +173,24 @@ def test_mlp_kernel_paths(name, path, tmp_path, monkeypatch):
         assert_close(out, ref.reshape(out.shape), f"{name} {path} n={n}")
 
 
-@pytest.mark.parametrize("path", ["tc", "tc_unfused", "ffma"])
+@pytest.mark.parametrize("path", ["default", "tc", "tc_unfused", "ffma"])
 @pytest.mark.parametrize("name", ["lstm", "lstm2"])
 def test_lstm_kernel_paths(name, path, tmp_path, monkeypatch):
-    """The LSTM kernels (tcgen05 3xTF32 per layer, the fused two-layer tcgen05
-    kernel, FFMA) on both LSTM workloads."""
-    monkeypatch.setenv("ROSENNA_LSTM_PATH", "ffma" if path == "ffma" else "tc")
+    """The LSTM kernels on both LSTM workloads: by default the dual-tile
+    tcgen05 kernel (4H = 128) and the fused two-layer tcgen05 kernel (H = 64);
+    the tcgen05 kernel that splits one tile's gates between the column groups,
+    with and without the two-layer fusion; the FFMA kernel."""
+    if path == "default":
+        monkeypatch.delenv("ROSENNA_LSTM_PATH", raising=False)
+    else:
+        monkeypatch.setenv("ROSENNA_LSTM_PATH", "ffma" if path == "ffma" else "tc")
     monkeypatch.setenv("ROSENNA_LSTM2_FUSE", "0" if path == "tc_unfused" else "1")
     workloads.write_model(name, str(tmp_path))
     api.initialize(str(tmp_path))
     desc = api.plan_description()
     assert ("lstm_tc" in desc) == (path != "ffma"), desc
-    assert ("lstm2_tc" in desc) == (name == "lstm2" and path == "tc"), desc
+    assert ("lstm_tc_dual" in desc) == (name == "lstm" and path == "default"), desc
+    assert ("lstm2_tc" in desc) == (name == "lstm2" and path in ("default", "tc")), desc
     for n in (1, 129, 1000, 4099):
         ins = workloads.make_inputs(name, n, seed_offset=3 + n)
         out = api.use_model_rows(ins)[0]
