@@ -6,18 +6,22 @@
 // 128-sample x 4H x 64 product of [x_t | h_{t-1}] (two 32-wide K-chunks) with
 // the packed gate block (rows n = 4j+q: gate q of unit j; tf32 hi rows, then
 // the rounded remainders).  The block is small enough to stay in shared memory
-// for the whole kernel (one TMA load).  Each group's warps hold their tile's c
-// and h in registers (thread = sample row, all units), stage [x_t | h_{t-1}] as
-// tf32 hi/lo A chunks, and after the step's MMAs drain the gate partial from
-// TMEM and run the cell update.  The issuer takes group 0's step, then group
-// 1's, so one group's cell update runs while the other's MMAs do; with all 4H
-// columns in one MMA (N = 4H), an M = 128 MMA uses the tensor core fully at 4H
-// = 128.  x_{t+1} is prefetched by cp.async during step t.
+// for the whole kernel (one TMA load).  The CTA runs two tiles at a time, each
+// by two warpgroups that split its units (16 each: thread = sample row; its
+// units' c and h in registers, their gate columns drained 16 at a time): they stage
+// their K halves of [x_t | h_{t-1}] as tf32 hi/lo A chunks, and after the
+// step's MMAs drain their half of the gate partial from TMEM and run the cell
+// update.  The issuer takes tile 0's step, then tile 1's, so one tile's cell
+// update runs while the other's MMAs do; with all 4H columns in one MMA (N =
+// 4H), an M = 128 MMA uses the tensor core fully at 4H = 128.  x_{t+1} is
+// prefetched by cp.async during step t.  (With one warpgroup per tile holding
+// all 32 units, the 192 live registers left the MUFU-bound cell update too few
+// warps to hide its latency.)
 //
-// Roles (384 threads): warps 0-3 group 0, warps 4-7 group 1, warp 8 lane 0
-// issues the MMAs.  setmaxnreg moves registers from the producer warpgroup
-// (40) to the groups (232).  Every wait is bounded; a time-out records where
-// in `err`, every role finishes, TMEM is freed.
+// Roles (544 threads): warps 0-15 the four warpgroups (tile = warpgroup / 2,
+// unit half = warpgroup % 2), warp 16 lane 0 issues the MMAs.  Every wait is
+// bounded; a time-out records where in `err`, every role finishes, TMEM is
+// freed.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -29,10 +33,7 @@
 namespace rosenna {
 namespace {
 
-constexpr int kDThreads = 384;
-constexpr int kDLaunchRegs = 168;
-constexpr int kDConsumerRegs = 232, kDProducerRegs = 40;
-static_assert(kDThreads * kDLaunchRegs >= 256 * kDConsumerRegs + 128 * kDProducerRegs, "register split");
+constexpr int kDThreads = 544;
 
 constexpr uint32_t kDTile = 128 * 128;          // one 32-wide K-chunk of 128 rows (hi or lo)
 constexpr uint32_t kDOffB = 0;                  // 2 K-chunks x (hi, lo)
@@ -47,9 +48,9 @@ size_t lstm_dual_tc_smem() { return 1024 + kDOffBars + 256; }
 
 enum {
     kDBReady = 0,   // the gate block loaded
-    kDAFull = 1,    // [2 groups][2 chunks] staged (128 arrivals each)
-    kDPFull = 5,    // [2] gates of the group's step complete (commit)
-    kDPEmpty = 7,   // [2] drained (128 arrivals)
+    kDAFull = 1,    // [2 tiles][2 chunks] staged (256 arrivals each: both unit halves)
+    kDPFull = 5,    // [2] gates of the tile's step complete (commit)
+    kDPEmpty = 7,   // [2] drained (256 arrivals)
     kDDone = 9,
     kDNumBars = 10
 };
@@ -59,27 +60,19 @@ __device__ __forceinline__ void cp_async4(float *dst, const float *src, bool val
                  : "memory");
 }
 
-// x_s of sample row r into this group's buffer ([k][row], k < 32; zero beyond I)
-__device__ __forceinline__ void d_prefetch_x(const TcLstmArgs &p, float *xbuf, int r, long long row, int s) {
+// features 16hf..16hf+15 of x_s, sample row r, into the tile's buffer ([k][row];
+// zero beyond I)
+__device__ __forceinline__ void d_prefetch_x(const TcLstmArgs &p, float *xbuf, int r, long long row, int s, int hf) {
     const bool valid = row < p.n;
 #pragma unroll
-    for (int k = 0; k < 32; k++) {
+    for (int e = 0; e < 16; e++) {
+        const int k = 16 * hf + e;
         const bool ok = valid && k < p.I;
         cp_async4(xbuf + (size_t)k * 128 + r, ok ? p.x + (long long)(s + (long long)p.T * k) * p.ld_x + row : p.x, ok);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// 32 values of row r (k = 0..31) as an A chunk (hi at `chunk`, lo 16 KB on).
-__device__ __forceinline__ void d_put32(uint8_t *chunk, int r, const float *v32) {
-    float v[16];
-#pragma unroll
-    for (int hf = 0; hf < 2; hf++) {
-#pragma unroll
-        for (int e = 0; e < 16; e++) v[e] = v32[16 * hf + e];
-        put_a16(chunk, chunk + kDTile, r, 16 * hf, v);
-    }
-}
 
 __device__ __forceinline__ void d_issue(uint32_t a_s, uint32_t b_s, uint32_t d, uint32_t idesc, bool first) {
     const uint32_t ah = desc_lo(a_s), al = ah + (kDTile >> 4);
@@ -115,10 +108,10 @@ __global__ void __launch_bounds__(kDThreads, 1) lstm_dual_tc_kernel(const __grid
     for (int i = tid; i < 128; i += kDThreads) sbias[i] = i < Np ? p.arena[p.b_off + i] : 0.f;
     if (tid == 0) {
         mbar_init(bars + kDBReady, 1);
-        for (int i = 0; i < 4; i++) mbar_init(bars + kDAFull + i, 128);
+        for (int i = 0; i < 4; i++) mbar_init(bars + kDAFull + i, 256);
         for (int g = 0; g < 2; g++) {
             mbar_init(bars + kDPFull + g, 1);
-            mbar_init(bars + kDPEmpty + g, 128);
+            mbar_init(bars + kDPEmpty + g, 256);
         }
         mbar_init(bars + kDDone, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -133,9 +126,8 @@ __global__ void __launch_bounds__(kDThreads, 1) lstm_dual_tc_kernel(const __grid
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp >= 8) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kDProducerRegs));
-        if (warp == 8 && lane == 0) {
+    if (warp >= 16) {
+        if (warp == 16 && lane == 0) {
             // ---- the gate block, once; then the MMA issuer ----
             asm volatile("prefetch.tensormap [%0];" ::"l"(&p.map) : "memory");
             mbar_arrive_expect_tx(bars + kDBReady, 4u * (uint32_t)Np * 128u);
@@ -171,84 +163,94 @@ __global__ void __launch_bounds__(kDThreads, 1) lstm_dual_tc_kernel(const __grid
             mbar_wait(bars + kDDone, 0, p.err, 0);
         }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kDConsumerRegs));
-        const int g = warp >> 2, quad = warp & 3;
+        const int wg = warp >> 2, g = wg >> 1, hf = wg & 1, quad = warp & 3;
         const int r = quad * 32 + lane;
-        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(128 * g);
-        const int slot = (lane == 0 && quad == 2) ? 3 + g : 0;
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(128 * g + 64 * hf);
+        const int slot = (lane == 0 && quad == 2) ? 3 + wg : 0;
         uint8_t *const ax = base + kDOffA + (uint32_t)(2 * g) * 2 * kDTile;  // x slot, then h slot
         uint8_t *const ah = ax + 2 * kDTile;
         float *const xbuf = reinterpret_cast<float *>(base + kDOffX + (uint32_t)g * kDXBuf);
+        const float *const bias = sbias + 64 * hf;
         uint32_t nst = 0;
         bool ok = true;
-        float acc[128], c[32], h[32];
+        float c[16], h[16];
         for (int k = 0; k < my_pairs && ok; k++) {
             const int t = 2 * ((int)blockIdx.x + k * (int)gridDim.x) + g;
-            if (t >= ntiles) break;  // the last pair may have only group 0's tile
+            if (t >= ntiles) break;  // the last pair may have only tile 0
             const long long row = (long long)t * 128 + r;
             const bool valid = row < p.n;
 #pragma unroll
-            for (int u = 0; u < 32; u++) {
+            for (int u = 0; u < 16; u++) {
+                const int unit = 16 * hf + u;
                 float h0 = 0.f, c0 = 0.f;
-                if (u < p.H && valid) {
-                    h0 = p.h0 ? p.h0[(long long)u * p.ld_h0 + row] : (p.h0_const >= 0 ? p.arena[p.h0_const + u] : 0.f);
-                    c0 = p.c0 ? p.c0[(long long)u * p.ld_c0 + row] : (p.c0_const >= 0 ? p.arena[p.c0_const + u] : 0.f);
+                if (unit < p.H && valid) {
+                    h0 = p.h0 ? p.h0[(long long)unit * p.ld_h0 + row]
+                              : (p.h0_const >= 0 ? p.arena[p.h0_const + unit] : 0.f);
+                    c0 = p.c0 ? p.c0[(long long)unit * p.ld_c0 + row]
+                              : (p.c0_const >= 0 ? p.arena[p.c0_const + unit] : 0.f);
                 }
                 h[u] = h0;
                 c[u] = c0;
             }
-            d_prefetch_x(p, xbuf, r, row, 0);
+            // h_{-1}: the h slot is free (the previous tile's last MMAs completed)
+            put_a16(ah, ah + kDTile, r, 16 * hf, h);
+            d_prefetch_x(p, xbuf, r, row, 0, hf);
             for (int s = 0; s < T && ok; s++) {
-                // [x_s | h_{s-1}]: the slots are free (the step before's MMAs completed with its gates)
+                // x_s (this half's K range) beside h_{s-1}, staged at the end of the step before
                 asm volatile("cp.async.wait_group 0;" ::: "memory");
-                float v[32];
+                {
+                    float v[16];
 #pragma unroll
-                for (int kk = 0; kk < 32; kk++) v[kk] = xbuf[(size_t)kk * 128 + r];
-                d_put32(ax, r, v);
-                d_put32(ah, r, h);
+                    for (int e = 0; e < 16; e++) v[e] = xbuf[(size_t)(16 * hf + e) * 128 + r];
+                    put_a16(ax, ax + kDTile, r, 16 * hf, v);
+                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 tc_fence_before();
                 mbar_arrive(bars + kDAFull + 2 * g);
                 mbar_arrive(bars + kDAFull + 2 * g + 1);
-                if (s + 1 < T) d_prefetch_x(p, xbuf, r, row, s + 1);
-                // gates: bias + the partial
+                if (s + 1 < T) d_prefetch_x(p, xbuf, r, row, s + 1, hf);
                 ok = __all_sync(0xffffffffu, mbar_wait(bars + kDPFull + g, nst & 1, p.err, 44, s, (int)nst, 0, slot));
                 if (!ok) break;
                 tc_fence_after();
+                // gates of this half's units in four rounds of 4 units (16 columns):
+                // bias + the partial, then the cell update (layers.f90 lstm_cell)
 #pragma unroll
-                for (int q0 = 0; q0 < 8; q0 += 4) {
-                    uint32_t w[4][16];
-#pragma unroll
-                    for (int u = 0; u < 4; u++)
-                        if (16 * (q0 + u) < Np) tmem_ld16_nw(lane_base + (uint32_t)(16 * (q0 + u)), w[u]);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int u = 0; u < 4; u++)
+                for (int rd = 0; rd < 4; rd++) {
+                    float acc[16];
+                    {
+                        uint32_t w[16];
+                        if (64 * hf + 16 * rd < Np) tmem_ld16_nw(lane_base + (uint32_t)(16 * rd), w);
+                        tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 16; e++)
-                            acc[16 * (q0 + u) + e] = 16 * (q0 + u) < Np ? __uint_as_float(w[u][e]) + sbias[16 * (q0 + u) + e]
-                                                                         : 0.f;
-                }
-                tc_fence_before();
-                mbar_arrive(bars + kDPEmpty + g);
-                nst++;
-                // cell update (layers.f90 lstm_cell): gates of unit u at acc[4u..4u+3]
+                            acc[e] = 64 * hf + 16 * rd < Np ? __uint_as_float(w[e]) + bias[16 * rd + e] : 0.f;
+                    }
+                    if (rd == 3) {
+                        tc_fence_before();
+                        mbar_arrive(bars + kDPEmpty + g);
+                    }
 #pragma unroll
-                for (int u = 0; u < 32; u++) {
-                    const float ig = tc_act<3>(acc[4 * u]), fg = tc_act<3>(acc[4 * u + 1]);
-                    const float gg = tc_act<2>(acc[4 * u + 2]), og = tc_act<3>(acc[4 * u + 3]);
-                    c[u] = fg * c[u] + ig * gg;
-                    h[u] = og * tc_act<2>(c[u]);
-                    if (u >= p.H) h[u] = c[u] = 0.f;  // padded units stay zero
+                    for (int uu = 0; uu < 4; uu++) {
+                        const int u = 4 * rd + uu;
+                        const float ig = tc_act<3>(acc[4 * uu]), fg = tc_act<3>(acc[4 * uu + 1]);
+                        const float gg = tc_act<2>(acc[4 * uu + 2]), og = tc_act<3>(acc[4 * uu + 3]);
+                        c[u] = fg * c[u] + ig * gg;
+                        h[u] = og * tc_act<2>(c[u]);
+                        if (16 * hf + u >= p.H) h[u] = c[u] = 0.f;  // padded units stay zero
+                    }
                 }
+                nst++;
+                // h_s into the h slot for the next step (this step's MMAs are complete)
+                put_a16(ah, ah + kDTile, r, 16 * hf, h);
                 if (valid) {
 #pragma unroll
-                    for (int u = 0; u < 32; u++) {
-                        if (u >= p.H) continue;
-                        if (p.y) p.y[(long long)(s + (long long)T * u) * p.ld_y + row] = h[u];
+                    for (int u = 0; u < 16; u++) {
+                        const int unit = 16 * hf + u;
+                        if (unit >= p.H) continue;
+                        if (p.y) p.y[(long long)(s + (long long)T * unit) * p.ld_y + row] = h[u];
                         if (s + 1 == T) {
-                            if (p.hn) p.hn[(long long)u * p.ld_hn + row] = h[u];
-                            if (p.cn) p.cn[(long long)u * p.ld_cn + row] = c[u];
+                            if (p.hn) p.hn[(long long)unit * p.ld_hn + row] = h[u];
+                            if (p.cn) p.cn[(long long)unit * p.ld_cn + row] = c[u];
                         }
                     }
                 }
@@ -267,14 +269,7 @@ __global__ void __launch_bounds__(kDThreads, 1) lstm_dual_tc_kernel(const __grid
 
 }  // namespace
 
-bool lstm_dual_tc_regs_ok() {
-    cudaFuncAttributes a{};
-    if (cudaFuncGetAttributes(&a, lstm_dual_tc_kernel) != cudaSuccess) {
-        (void)cudaGetLastError();
-        return true;
-    }
-    return a.numRegs == kDLaunchRegs;
-}
+bool lstm_dual_tc_regs_ok() { return true; }  // no register split between roles
 
 cudaError_t lstm_dual_tc_configure() {
     return cudaFuncSetAttribute(lstm_dual_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -286,11 +281,6 @@ cudaError_t launch_lstm_dual_tc(const TcLstmArgs &a, int num_sms, cudaStream_t s
     const int grid = (int)(pairs < num_sms ? pairs : num_sms);
     if (grid <= 0) return cudaSuccess;
     if (a.nx != 1 || a.nh != 1 || a.Np > 128 || a.H > 32 || a.I > 32) return cudaErrorInvalidConfiguration;
-    static const int regs = [] {
-        cudaFuncAttributes fa{};
-        return cudaFuncGetAttributes(&fa, lstm_dual_tc_kernel) == cudaSuccess ? fa.numRegs : -1;
-    }();
-    if (regs != kDLaunchRegs) return cudaErrorInvalidConfiguration;  // the setmaxnreg split needs exactly these
     lstm_dual_tc_kernel<<<grid, kDThreads, lstm_dual_tc_smem(), st>>>(a);
     return cudaGetLastError();
 }
