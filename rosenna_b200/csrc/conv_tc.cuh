@@ -2,46 +2,55 @@
 // and a 2x2 pool: parameter block, weight packing and launcher.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
 
 namespace rosenna {
 
-// The B image (floats): up to 4 K-chunks, each tf32 hi then lo parts of
-// [64 rows x 32] (rows = pixel*OCp + oc over the block's patch).
-constexpr int kConvTcBChunk = 2 * 64 * 32;
-constexpr int kConvTcBFloats = 4 * kConvTcBChunk;
+// The weight image (floats): the sliding-window weight matrix, 288 rows x 32
+// K-slots, tf32 hi part then lo part, each in the 128-byte-swizzled K-major
+// layout the kernel copies to shared memory as it is.
+constexpr int kConvTcRows = 288;
+constexpr int kConvTcBFloats = 2 * kConvTcRows * 32;
 
-// How a conv maps onto the kernel: channels per patch position in K (8, or 1
-// for a single-channel input), pooled windows per block (1 with 16 output
-// channels, 2 with 8), 32-wide K-chunks per block.
+// How a conv maps onto the kernel.  A block is bh x 4 conv pixels (rows y x
+// columns x) times ocp output channels = 128 GEMM rows; its input patch is
+// (bh + 2) x 6 positions, loaded as ph rows (>= bh + 2) of cb channels (C
+// rounded up to 1, 2, 4 or 8; the extra channels read as zeros) per column,
+// cw columns per chunk (rows = cb * ph * cw K-rows).
 struct ConvTcGeom {
-    int cp, bwin, nch;
+    int ocp, bh, cb, ph, cw, rows, slots;
+    bool ok;
 };
 ConvTcGeom conv_tc_geometry(int C, int OC);
 
 struct ConvTcArgs {
+    CUtensorMap map;          // the input as {samples, cb of C channels, Hin, Win}, box {32, cb, ph, cw}
     const float *arena;
-    long long bt_off, b_off;  // arena offsets: the B image, bias[OC]
-    const float *in;          // input element (c, y, x) at row c + C*(y + Hin*x)
-    long long ld_in;
+    long long bt_off, b_off;  // arena offsets: the weight image, bias[OC]
     float *out;               // output (oc, qy, qx) at row oc*so_c + qy*so_h + qx*so_w
     long long ld_out, so_c, so_h, so_w;
     long long n;
     int *err;                 // [64] status word shared with the other tensor-core kernels
-    int C, Hin, Win, pad, OC, Hq, Wq, pool, relu;  // pool: 1 max, 2 avg (k = s = 2)
-    int cp, bwin, nch;        // conv_tc_geometry(C, OC)
+    int C, Hin, Win, pad, OC, Ho, Wo, Hq, Wq, pool, relu;  // pool: 1 max, 2 avg (k = s = 2)
+    int ocp, bh, cb, ph, cw, rows, slots;                  // conv_tc_geometry(C, OC)
+    int vec_out;              // out and ld_out allow 16-byte stores
 };
 
 // Whether a conv(+ReLU)+pool step has the shapes conv_tc_kernel covers.
 bool conv_tc_shape_ok(int KS, int str_h, int str_w, int pad_h, int pad_w, int C, int OC, int pool, int pk, int pstr_h,
                       int pstr_w, int ppad_h, int ppad_w, int Ho, int Wo);
-// Packs 3x3 weights w[oc][ic][kh][kw] (OC <= 16, C <= 8) into the B image
-// (kConvTcBFloats floats): the weights laid out over the block's patch, tf32 hi
-// and lo parts, in the 128-byte-swizzled K-major layout the kernel copies to
-// shared memory.
+// Packs 3x3 weights w[oc][ic][kh][kw] (OC <= 16, C <= 8) into the weight image
+// (kConvTcBFloats floats).
 void conv_tc_pack(const float *w, int OC, int C, float *img);
+// Whether an input array can be read by the kernel's tensor map (16-byte
+// aligned base and sample pitch).
+bool conv_tc_input_ok(const float *in, long long ld_in);
+// Encodes a.map for the input `in` (element (c, y, x) of sample s at
+// in[(c + C*(y + Hin*x))*ld_in + s]) from the geometry fields of `a`.
+bool conv_tc_encode_input(ConvTcArgs &a, const float *in, long long ld_in, const char **why);
 cudaError_t conv_tc_configure();
 cudaError_t launch_conv_tc(const ConvTcArgs &a, int num_sms, cudaStream_t st);
 

@@ -1311,7 +1311,8 @@ cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st) {
 
 namespace rosenna {
 
-bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, const char **why, int box_rows) {
+bool tc_encode_f32_map(CUtensorMap *map, int rank, const void *base, const cuuint64_t *dims, const cuuint64_t *strides,
+                       const cuuint32_t *box, const char **why, CUtensorMapSwizzle swizzle) {
     typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -1326,18 +1327,22 @@ bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, con
         }
         encode = reinterpret_cast<EncodeFn>(fn);
     }
-    const cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)(2 * Np)};
-    const cuuint64_t strides[1] = {(cuuint64_t)Kp * sizeof(float)};
-    const cuuint32_t box[2] = {32, (cuuint32_t)(box_rows > 0 ? box_rows : Np)};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(block), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void *>(base), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
-        *why = "cuTensorMapEncodeTiled rejected a weight block";
+        *why = "cuTensorMapEncodeTiled rejected a tensor map";
         return false;
     }
     return true;
+}
+
+bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, const char **why, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)(2 * Np)};
+    const cuuint64_t strides[1] = {(cuuint64_t)Kp * sizeof(float)};
+    const cuuint32_t box[2] = {32, (cuuint32_t)(box_rows > 0 ? box_rows : Np)};
+    return tc_encode_f32_map(map, 2, block, dims, strides, box, why);
 }
 
 }  // namespace rosenna

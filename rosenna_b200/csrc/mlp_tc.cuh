@@ -104,6 +104,14 @@ cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
 // boxes of {32, box_rows} (box_rows 0: Np).  Returns false (with *why set) when
 // the driver entry point or encode fails.
 bool mlp_tc_encode_map(CUtensorMap *map, const float *block, int Kp, int Np, const char **why, int box_rows = 0);
+// Encodes a tiled fp32 TMA map of `rank` dimensions (dims innermost first,
+// strides in bytes for dims 1..rank-1), zero fill out of bounds, 128-byte
+// swizzle (CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B for an operand the MMA reads
+// MN-major).  Returns false (with *why set) when the driver entry point or
+// encode fails.
+bool tc_encode_f32_map(CUtensorMap *map, int rank, const void *base, const cuuint64_t *dims, const cuuint64_t *strides,
+                       const cuuint32_t *box, const char **why,
+                       CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // One LSTM layer with I <= 32, H <= 32 (4H <= 128), each column group running
 // a tile of its own (lstm_dual_tc.cu); TcLstmArgs as for launch_lstm_tc.

@@ -316,22 +316,28 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 break;
             }
             case Step::CONV: {
-                if (s.tc) {
+                // the tensor-core conv reads its input through a TMA map: a
+                // 16-byte aligned base and sample pitch (otherwise the CUDA-core
+                // kernel below takes the call)
+                if (s.tc && conv_tc_input_ok(ptr[(size_t)s.in], ld[(size_t)s.in])) {
                     ConvTcArgs a{};
                     a.arena = arena;
                     a.bt_off = s.ctc_off;
                     a.b_off = s.b_off;
-                    a.in = ptr[(size_t)s.in];
-                    a.ld_in = ld[(size_t)s.in];
                     a.out = ptr[(size_t)s.out];
                     a.ld_out = ld[(size_t)s.out];
                     a.so_c = s.so_c; a.so_h = s.so_h; a.so_w = s.so_w;
                     a.n = cnt;
                     a.err = d.err;
                     a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.pad = s.pad_h; a.OC = s.OC;
-                    a.Hq = s.Hq; a.Wq = s.Wq; a.pool = s.pool; a.relu = s.relu ? 1 : 0;
+                    a.Ho = s.Ho; a.Wo = s.Wo; a.Hq = s.Hq; a.Wq = s.Wq; a.pool = s.pool; a.relu = s.relu ? 1 : 0;
                     const ConvTcGeom geo = conv_tc_geometry(s.C, s.OC);
-                    a.cp = geo.cp; a.bwin = geo.bwin; a.nch = geo.nch;
+                    a.ocp = geo.ocp; a.bh = geo.bh; a.cb = geo.cb; a.ph = geo.ph; a.cw = geo.cw;
+                    a.rows = geo.rows; a.slots = geo.slots;
+                    a.vec_out = ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ld_out & 3) == 0) ? 1 : 0;
+                    const char *why = nullptr;
+                    if (!conv_tc_encode_input(a, ptr[(size_t)s.in], ld[(size_t)s.in], &why))
+                        return Status::Err(ROSENNA_ERR_CUDA, std::string("conv_tc input map: ") + (why ? why : "?"));
                     e = launch_conv_tc(a, d.num_sms, stream);
                     launches++;
                     if (e == cudaSuccess)

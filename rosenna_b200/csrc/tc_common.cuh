@@ -85,6 +85,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     __threadfence();
     return false;
 }
+// Bounded wait that does not stop at a recorded error: at exit, for copies a
+// role issued that may still be in flight.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 0; i < kWaitIters; i++) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((i & 255) == 255 && globaltimer() - t0 > kWaitNs) return;
+    }
+}
 
 // ---- TMA -------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
@@ -92,6 +101,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
             smem_u32(dst)),
         "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// 4-D tile {c0 innermost, c1, c2, c3}; coordinates past either end of a
+// dimension read as zeros
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
 
@@ -224,6 +244,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 // version 1, 128-byte swizzle): one register per descriptor.
 constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
 __device__ __forceinline__ uint32_t desc_lo(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+// An MN-major 32-bit operand must use the 128-byte swizzle with 32-byte atoms
+// (layout type 1, written by TMA maps of CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B):
+// atoms of 32 MN-elements (128 B) x 4 K-rows.  Low word: start address and
+// `mn_stride` bytes between consecutive 32-element MN groups (the leading byte
+// offset); high word: 512 B between 4-row K groups, version 1, layout type 1.
+constexpr uint32_t kDescHiMN32 = (512u >> 4) | (1u << 14) | (1u << 29);
+__device__ __forceinline__ uint32_t desc_mn_lo(uint32_t saddr, uint32_t mn_stride) {
+    return ((saddr & 0x3FFFFu) >> 4) | ((mn_stride >> 4) << 16);
+}
+// instruction descriptor: D f32, A tf32 K-major, B tf32 MN-major, M=128, N
+__device__ __forceinline__ uint32_t idesc_tf32_bmn(int N) { return idesc_tf32(N) | (1u << 16); }
 __device__ __forceinline__ void umma_tf32_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
                                              uint32_t acc) {
     asm volatile(
@@ -233,6 +264,17 @@ __device__ __forceinline__ void umma_tf32_lo(uint32_t d_tmem, uint32_t a_lo, uin
         "mov.b64 db, {%2, %5};\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
         "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(acc), "n"(kDescHi));
+}
+// The same with B MN-major (b_lo from desc_mn_lo, idesc from idesc_tf32_bmn).
+__device__ __forceinline__ void umma_tf32_bmn(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                              uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "mov.b64 da, {%1, %5};\n\t"
+        "mov.b64 db, {%2, %6};\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(acc), "n"(kDescHi), "n"(kDescHiMN32));
 }
 
 }  // namespace
