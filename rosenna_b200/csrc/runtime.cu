@@ -316,10 +316,11 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 break;
             }
             case Step::CONV: {
-                // the tensor-core conv reads its input through a TMA map: a
-                // 16-byte aligned base and sample pitch (otherwise the CUDA-core
-                // kernel below takes the call)
-                if (s.tc && conv_tc_input_ok(ptr[(size_t)s.in], ld[(size_t)s.in])) {
+                // the tensor-core conv reads its input and writes its output
+                // through TMA maps: 16-byte aligned bases and sample pitches
+                // (otherwise the CUDA-core kernel below takes the call)
+                if (s.tc && conv_tc_input_ok(ptr[(size_t)s.in], ld[(size_t)s.in]) &&
+                    conv_tc_input_ok(ptr[(size_t)s.out], ld[(size_t)s.out])) {
                     ConvTcArgs a{};
                     a.arena = arena;
                     a.bt_off = s.ctc_off;
@@ -334,10 +335,11 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                     const ConvTcGeom geo = conv_tc_geometry(s.C, s.OC);
                     a.ocp = geo.ocp; a.bh = geo.bh; a.cb = geo.cb; a.ph = geo.ph; a.cw = geo.cw;
                     a.rows = geo.rows; a.slots = geo.slots;
-                    a.vec_out = ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ld_out & 3) == 0) ? 1 : 0;
                     const char *why = nullptr;
                     if (!conv_tc_encode_input(a, ptr[(size_t)s.in], ld[(size_t)s.in], &why))
                         return Status::Err(ROSENNA_ERR_CUDA, std::string("conv_tc input map: ") + (why ? why : "?"));
+                    if (!conv_tc_encode_output(a, &why))
+                        return Status::Err(ROSENNA_ERR_CUDA, std::string("conv_tc output map: ") + (why ? why : "?"));
                     e = launch_conv_tc(a, d.num_sms, stream);
                     launches++;
                     if (e == cudaSuccess)

@@ -95,6 +95,18 @@ __device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// Named barrier `id` over `nthreads` threads that also returns the AND of
+// every participant's `v`, so a group of warps leaves a loop together.
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // ---- TMA -------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
     asm volatile(
@@ -113,6 +125,26 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
         "[%2];" ::"r"(smem_u32(dst)),
         "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
+}
+
+// 4-D tile store from shared memory (bulk-group completion); parts of the box
+// past the end of a dimension are not written.  Coordinates must not be
+// negative.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(map),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// waits until at most N committed bulk groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// waits until at most N committed bulk groups are incomplete
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ---- tcgen05 ----------------------------------------------------------------
@@ -244,17 +276,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 // version 1, 128-byte swizzle): one register per descriptor.
 constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
 __device__ __forceinline__ uint32_t desc_lo(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
-// An MN-major 32-bit operand must use the 128-byte swizzle with 32-byte atoms
-// (layout type 1, written by TMA maps of CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B):
-// atoms of 32 MN-elements (128 B) x 4 K-rows.  Low word: start address and
-// `mn_stride` bytes between consecutive 32-element MN groups (the leading byte
-// offset); high word: 512 B between 4-row K groups, version 1, layout type 1.
-constexpr uint32_t kDescHiMN32 = (512u >> 4) | (1u << 14) | (1u << 29);
-__device__ __forceinline__ uint32_t desc_mn_lo(uint32_t saddr, uint32_t mn_stride) {
-    return ((saddr & 0x3FFFFu) >> 4) | ((mn_stride >> 4) << 16);
-}
-// instruction descriptor: D f32, A tf32 K-major, B tf32 MN-major, M=128, N
-__device__ __forceinline__ uint32_t idesc_tf32_bmn(int N) { return idesc_tf32(N) | (1u << 16); }
 __device__ __forceinline__ void umma_tf32_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
                                              uint32_t acc) {
     asm volatile(
@@ -265,16 +286,35 @@ __device__ __forceinline__ void umma_tf32_lo(uint32_t d_tmem, uint32_t a_lo, uin
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
         "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(acc), "n"(kDescHi));
 }
-// The same with B MN-major (b_lo from desc_mn_lo, idesc from idesc_tf32_bmn).
-__device__ __forceinline__ void umma_tf32_bmn(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
-                                              uint32_t acc) {
+// The same with A read from TMEM (a_tmem: the column of its first K element,
+// lanes 0..127 = the M rows) and B from shared memory (K-major, 128-byte
+// swizzle, b_lo from desc_lo).
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
+                                             uint32_t acc) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+        "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "mov.b64 da, {%1, %5};\n\t"
-        "mov.b64 db, {%2, %6};\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(acc), "n"(kDescHi), "n"(kDescHiMN32));
+        "mov.b64 db, {%2, %5};\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], db, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(acc), "n"(kDescHi));
+}
+
+// 32 lanes x 32 bits, 8 consecutive columns per thread
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+// 32 lanes x 32 bits, 32 consecutive columns per thread (no wait)
+__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
 }
 
 }  // namespace
