@@ -1,0 +1,390 @@
+// Tensor-core MLP for narrow chains whose weights fit in shared memory (every
+// tensor-core layer at most 64 wide, at most 64 inputs), 3xTF32 on tcgen05
+// (fLibrary/layers.f90:11-23 linear_layer, activation_funcs.f90 per layer).
+//
+// Math as in mlp_tc.cu: Y = act(A W^T + b) with A = Ah + Al, W = Wh + Wl taken
+// as Al*Wh + Ah*Wl + Ah*Wh, accumulated in fp32 in TMEM.
+//
+// Per CTA (one per SM, persistent): two 128-sample tiles at a time, one per
+// warpgroup (thread = sample = TMEM lane).  Every layer's [Wh | Wl] K-chunks
+// are loaded once by TMA and stay in shared memory (the B operand).  The A
+// operand lives in TMEM: the warpgroup splits the tile's inputs, and after each
+// layer its own activations, into tf32 hi and lo parts and stores them into its
+// A region, so activations never pass through shared memory and the
+// shared-memory port carries only the weights the MMAs read.  One lane issues
+// every MMA, layer by layer, tile 0's then tile 1's, so one tile's epilogue
+// (bias, activation, split) runs while the other tile's MMAs do.  A narrow last
+// layer (N <= 16) runs on the CUDA cores straight from the registers of the
+// layer before.  With each layer's K-step loop unrolled (immediate descriptor
+// offsets), the MMAs issue back to back.
+//
+// TMEM per tile (256 columns at 256g): A hi at +0, A lo at +64, the layer's
+// accumulator at +128 (up to 64 columns).  A layer's MMAs read A while they
+// write the accumulator; the epilogue reads the accumulator (all of it, into
+// registers) before it writes the next layer's A, and the MMAs that read the
+// old A are complete by then (the accumulator's commit).
+//
+// Roles (288 threads): warps 0-3 tile group 0, warps 4-7 tile group 1, warp 8
+// lane 0 loads the weights and issues the MMAs.  Every wait is bounded; a
+// time-out records where in `err`, every role finishes, TMEM is freed.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "mlp_tc.cuh"
+#include "tc_common.cuh"
+
+namespace rosenna {
+namespace {
+
+constexpr int kNThreads = 288;
+constexpr int kNMaxK = 64;                     // widest A (inputs of a tensor-core layer)
+constexpr int kNMaxN = 64;                     // widest tensor-core layer
+constexpr uint32_t kNTmemCols = 512;
+constexpr uint32_t kNSmemW = 160 * 1024;       // resident weight blocks
+constexpr uint32_t kNSmemBias = kTcMaxLayers * kNMaxN * 4;
+constexpr uint32_t kNSmemTail = kNMaxK * kTcTailMaxN * 4 + kTcTailMaxN * 4;
+
+enum {
+    kNWReady = 0,   // the weights landed (TMA bytes)
+    kNAFull = 1,    // [2] the tile's A operand written (128 arrivals)
+    kNDFull = 3,    // [2] the tile's layer accumulator complete (commit)
+    kNDone = 5,
+    kNNumBars = 6
+};
+
+size_t mlp_narrow_smem() { return 1024 + kNSmemW + kNSmemBias + kNSmemTail + 8 * kNNumBars + 16; }
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// Splits 16 values into tf32 hi/lo and stores them at A columns c0.. (hi) and
+// 64 + c0.. (lo) of this thread's lane.
+__device__ __forceinline__ void n_put_a16(uint32_t lane_a, int c0, const float (&v)[16]) {
+    uint32_t h[16], l[16];
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+        h[e] = tf32_rna(v[e]);
+        l[e] = tf32_rna(v[e] - __uint_as_float(h[e]));
+    }
+    tmem_st16u(lane_a + (uint32_t)c0, h);
+    tmem_st16u(lane_a + 64u + (uint32_t)c0, l);
+}
+
+// Byte offset of layer l's weight chunks in the resident block (hi then lo of
+// each 32-wide K-chunk, Np rows of 128 bytes each).
+__device__ __forceinline__ uint32_t n_w_off(const TcArgs &p, int l) {
+    uint32_t off = 0;
+    for (int i = 0; i < l; i++) off += (uint32_t)p.L[i].nch * 2u * (uint32_t)p.L[i].Np * 128u;
+    return off;
+}
+
+// Layer l of one tile: up to 8 K-steps (K <= 64), three MMAs each, unrolled.
+__device__ __forceinline__ void n_issue_layer(uint32_t d, uint32_t a, uint32_t wh, uint32_t np, int ksteps,
+                                              uint32_t idesc) {
+    const uint32_t lo = (np * 128u) >> 4;  // the lo half of a chunk, in descriptor units
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (j < ksteps) {
+            // chunk j/4 (2*np rows of 128 B), 32 bytes per K-step within it
+            const uint32_t bh = wh + (uint32_t)(j >> 2) * ((2u * np * 128u) >> 4) + (uint32_t)((j & 3) * 2);
+            umma_tf32_ts(d, a + 64u + 8u * j, bh, idesc, j ? 1u : 0u);
+            umma_tf32_ts(d, a + 8u * j, bh + lo, idesc, 1u);
+            umma_tf32_ts(d, a + 8u * j, bh, idesc, 1u);
+        }
+    }
+}
+
+// Layer end into the next layer's A: bias, activation, tf32 split, for the
+// layer's np (<= 64, a multiple of 16) accumulator columns.  Columns at and
+// beyond N hold act(0) and meet zero weight columns in the next layer.
+template <int ACT>
+__device__ __forceinline__ void n_layer_to_a(uint32_t lane_d, uint32_t lane_a, const float *bias, int np) {
+#pragma unroll
+    for (int hq = 0; hq < 2; hq++) {  // 32 columns at a time
+        if (32 * hq >= np) break;
+        uint32_t v[2][16];
+        tmem_ld16_nw(lane_d + 32u * hq, v[0]);
+        if (32 * hq + 16 < np) tmem_ld16_nw(lane_d + 32u * hq + 16u, v[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const int c0 = 32 * hq + 16 * q;
+            if (c0 >= np) break;
+            float y[16];
+#pragma unroll
+            for (int e = 0; e < 16; e++) y[e] = tc_act<ACT>(__uint_as_float(v[q][e]) + bias[c0 + e]);
+            n_put_a16(lane_a, c0, y);
+        }
+    }
+}
+
+// The last tensor-core layer's activations, 16 columns at a time, straight
+// into the CUDA-core last layer: o[n] += act(acc[k] + b[k]) W^T[k][n] over the
+// zero-padded W^T in shared memory (rows at and beyond np never reached).
+template <int ACT, int TNP>
+__device__ __forceinline__ void n_layer_tail(uint32_t lane_d, const float *bias, int np, const float *tw,
+                                             float (&o)[TNP]) {
+#pragma unroll
+    for (int n = 0; n < TNP; n++) o[n] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        if (16 * q >= np) break;
+        uint32_t v[16];
+        tmem_ld16_nw(lane_d + 16u * q, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            const int k = 16 * q + e;
+            const float h = tc_act<ACT>(__uint_as_float(v[e]) + bias[k]);
+            const float4 *w = reinterpret_cast<const float4 *>(tw + k * kTcTailMaxN);
+#pragma unroll
+            for (int n4 = 0; n4 < TNP / 4; n4++) {
+                const float4 c = w[n4];
+                o[4 * n4] = fmaf(h, c.x, o[4 * n4]);
+                o[4 * n4 + 1] = fmaf(h, c.y, o[4 * n4 + 1]);
+                o[4 * n4 + 2] = fmaf(h, c.z, o[4 * n4 + 2]);
+                o[4 * n4 + 3] = fmaf(h, c.w, o[4 * n4 + 3]);
+            }
+        }
+    }
+}
+
+// The tail's bias, activation and output row.
+template <int TNP, int ACT>
+__device__ __forceinline__ void n_tail_out_act(const TcArgs &p, const float (&o)[TNP], const float *tb, long long row) {
+#pragma unroll
+    for (int n = 0; n < TNP; n++)
+        if (n < p.tail_n) p.out[row + (long long)n * p.ld_out] = tc_act<ACT>(o[n] + tb[n]);
+}
+template <int TNP>
+__device__ __forceinline__ void n_tail_out(const TcArgs &p, const float (&o)[TNP], const float *tb, long long row) {
+    if (row >= p.n) return;
+    switch (p.tail_act) {
+        case 1: n_tail_out_act<TNP, 1>(p, o, tb, row); break;
+        case 2: n_tail_out_act<TNP, 2>(p, o, tb, row); break;
+        case 3: n_tail_out_act<TNP, 3>(p, o, tb, row); break;
+        default: n_tail_out_act<TNP, 0>(p, o, tb, row); break;
+    }
+}
+
+// The last layer on the tensor cores (no CUDA-core tail): its outputs.
+template <int ACT>
+__device__ __forceinline__ void n_layer_out(const TcArgs &p, uint32_t lane_d, const float *bias, int np, int nout,
+                                            long long row) {
+    uint32_t v[4][16];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        if (16 * q < np) tmem_ld16_nw(lane_d + 16u * q, v[q]);
+    tmem_wait_ld();
+    if (row >= p.n) return;
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+#pragma unroll
+        for (int e = 0; e < 16; e++)
+            if (16 * q + e < nout) p.out[row + (long long)(16 * q + e) * p.ld_out] = tc_act<ACT>(__uint_as_float(v[q][e]) + bias[16 * q + e]);
+}
+
+// HACT: the activation of every tensor-core layer; TNP: the CUDA-core last
+// layer's padded width (8 or 16), 0 when the last layer is on the tensor cores.
+template <int HACT, int TNP>
+__global__ void __launch_bounds__(kNThreads, 1) mlp_narrow_tc_kernel(const __grid_constant__ TcArgs p) {
+    extern __shared__ uint8_t sm_raw[];
+    uint8_t *const wsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~(uintptr_t)1023);
+    float *const sbias = reinterpret_cast<float *>(wsm + kNSmemW);  // [layer][64]
+    float *const stw = sbias + kTcMaxLayers * kNMaxN;                // tail W^T [64][16], zero padded
+    float *const stb = stw + kNMaxK * kTcTailMaxN;                   // tail bias [16]
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(stb + kTcTailMaxN);
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + kNNumBars);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nl = p.nlayers;
+    const long long ntiles = (p.n + 127) / 128;
+
+    // biases and the tail's weights (plain loads; every thread)
+    for (int i = tid; i < nl * kNMaxN; i += kNThreads) {
+        const int l = i / kNMaxN, c = i - l * kNMaxN;
+        sbias[i] = c < p.L[l].Np ? p.arena[p.L[l].b_off + c] : 0.f;
+    }
+    for (int i = tid; i < kNMaxK * kTcTailMaxN; i += kNThreads) {
+        const int k = i / kTcTailMaxN, c = i - k * kTcTailMaxN;
+        stw[i] = (p.tail_n > 0 && k < p.tail_kp && c < p.tail_np) ? p.arena[p.tail_w_off + (long long)k * p.tail_np + c]
+                                                                   : 0.f;
+    }
+    if (tid < kTcTailMaxN) stb[tid] = (p.tail_n > 0 && tid < p.tail_np) ? p.arena[p.tail_b_off + tid] : 0.f;
+    if (tid == 0) {
+        mbar_init(bars + kNWReady, 1);
+        for (int g = 0; g < 2; g++) {
+            mbar_init(bars + kNAFull + g, 128);
+            mbar_init(bars + kNDFull + g, 1);
+        }
+        mbar_init(bars + kNDone, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kNTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            // ---- the weights, then every MMA ----
+            uint32_t bytes = 0;
+            for (int l = 0; l < nl; l++) bytes += (uint32_t)p.L[l].nch * 2u * (uint32_t)p.L[l].Np * 128u;
+            mbar_arrive_expect_tx(bars + kNWReady, bytes);
+            for (int l = 0; l < nl; l++) {
+                uint8_t *dst = wsm + n_w_off(p, l);
+                const uint32_t half = (uint32_t)p.L[l].Np * 128u;
+                for (int c = 0; c < p.L[l].nch; c++) {
+                    tma_load_2d(dst + c * 2 * half, &p.maps[l], bars + kNWReady, c * 32, 0);
+                    tma_load_2d(dst + c * 2 * half + half, &p.maps[l], bars + kNWReady, c * 32, p.L[l].Np);
+                }
+            }
+            bool ok = mbar_wait(bars + kNWReady, 0, p.err, 81);
+            const uint32_t wbase = desc_lo(smem_u32(wsm));
+            uint32_t acnt0 = 0, acnt1 = 0;
+            for (long long k = 0; ok; k++) {
+                const long long t0 = blockIdx.x + 2 * k * gridDim.x;
+                if (t0 >= ntiles) break;
+                const int ng = t0 + gridDim.x < ntiles ? 2 : 1;
+                uint32_t woff = 0;
+                for (int l = 0; l < nl && ok; l++) {
+                    const uint32_t np = (uint32_t)p.L[l].Np, idesc = idesc_tf32((int)np);
+                    const int ksteps = (p.L[l].K + 7) / 8;
+                    for (int g = 0; g < ng && ok; g++) {
+                        const uint32_t ac = g ? acnt1 : acnt0;
+                        if (!(ok = mbar_wait(bars + kNAFull + g, ac & 1, p.err, 82, (int)k, l, g))) break;
+                        if (g) acnt1++;
+                        else acnt0++;
+                        tc_fence_after();
+                        const uint32_t a = tmem + 256u * g;
+                        n_issue_layer(a + 128u, a, wbase + (woff >> 4), np, ksteps, idesc);
+                        umma_commit(bars + kNDFull + g);
+                    }
+                    woff += (uint32_t)p.L[l].nch * 2u * np * 128u;
+                }
+            }
+            umma_commit(bars + kNDone);
+            mbar_drain(bars + kNDone, 0);
+        }
+    } else {
+        // ---- tile groups: thread = sample row ----
+        const int g = warp >> 2, r = 32 * (warp & 3) + lane;
+        const uint32_t lane_a = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 256u * g, lane_d = lane_a + 128u;
+        const int k0 = p.L[0].K;
+        uint32_t dcnt = 0;
+        bool ok = true;
+        for (long long k = 0; ok; k++) {
+            const long long t = blockIdx.x + (2 * k + g) * gridDim.x;
+            if (t >= ntiles) break;
+            const long long row = t * 128 + r;
+            {  // layer 0's A: the inputs, zero beyond K (and past the batch)
+                const bool valid = row < p.n;
+#pragma unroll
+                for (int q = 0; q < kNMaxK / 16; q++)
+                    if (16 * q < k0) {
+                        float y[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            const int f = 16 * q + e;
+                            y[e] = (valid && f < k0) ? __ldg(p.in + (long long)f * p.ld_in + row) : 0.f;
+                        }
+                        n_put_a16(lane_a, 16 * q, y);
+                    }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                mbar_arrive(bars + kNAFull + g);
+            }
+            for (int l = 0; l < nl; l++) {
+                ok = __all_sync(0xffffffffu, mbar_wait(bars + kNDFull + g, dcnt & 1, p.err, 83, (int)k, l));
+                dcnt++;
+                if (!ok) break;
+                tc_fence_after();
+                const float *bias = sbias + l * kNMaxN;
+                const int np = p.L[l].Np;
+                if (l + 1 < nl) {
+                    n_layer_to_a<HACT>(lane_d, lane_a, bias, np);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    mbar_arrive(bars + kNAFull + g);
+                } else if constexpr (TNP > 0) {
+                    float o[TNP];
+                    n_layer_tail<HACT, TNP>(lane_d, bias, np, stw, o);
+                    n_tail_out<TNP>(p, o, stb, row);
+                } else {
+                    n_layer_out<HACT>(p, lane_d, bias, np, p.L[l].N, row);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kNTmemCols));
+    }
+}
+
+}  // namespace
+
+bool mlp_narrow_fits(const TcArgs &a) {
+    if (a.nlayers < 1 || a.nlayers > kTcMaxLayers) return false;
+    uint32_t bytes = 0;
+    for (int l = 0; l < a.nlayers; l++) {
+        const TcLayer &L = a.L[l];
+        if (L.act != a.L[0].act || L.act < 0 || L.act > 3) return false;  // one activation for every layer
+        if (L.Np > kNMaxN || L.Np % 16 || L.K > kNMaxK || L.K < 1 || L.nch < 1 || L.nch > 2) return false;
+        if (l > 0 && L.K > a.L[l - 1].Np) return false;
+        bytes += (uint32_t)L.nch * 2u * (uint32_t)L.Np * 128u;
+    }
+    if (bytes > kNSmemW) return false;
+    if (a.tail_n > 0 && (a.tail_np > kTcTailMaxN || a.tail_kp > kNMaxK || a.tail_k > a.L[a.nlayers - 1].Np))
+        return false;
+    return true;
+}
+
+#define ROSENNA_NARROW_VARIANTS(X) X(0, 0) X(1, 0) X(2, 0) X(3, 0) X(0, 8) X(1, 8) X(2, 8) X(3, 8) X(0, 16) X(1, 16) X(2, 16) X(3, 16)
+
+cudaError_t mlp_narrow_configure() {
+    cudaError_t e = cudaSuccess;
+#define ROSENNA_NARROW_CFG(A, T)                                                                          \
+    if (e == cudaSuccess)                                                                                 \
+        e = cudaFuncSetAttribute(mlp_narrow_tc_kernel<A, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 (int)mlp_narrow_smem());
+    ROSENNA_NARROW_VARIANTS(ROSENNA_NARROW_CFG)
+#undef ROSENNA_NARROW_CFG
+    return e;
+}
+
+cudaError_t launch_mlp_narrow(const TcArgs &a, int num_sms, cudaStream_t st) {
+    if (!mlp_narrow_fits(a)) return cudaErrorInvalidConfiguration;
+    const long long tiles = (a.n + 127) / 128, pairs = (tiles + 1) / 2;
+    const int grid = (int)(pairs < num_sms ? pairs : num_sms);
+    if (grid <= 0) return cudaSuccess;
+    const int act = a.L[0].act, tnp = a.tail_n > 0 ? (a.tail_np <= 8 ? 8 : 16) : 0;
+    bool launched = false;
+#define ROSENNA_NARROW_LAUNCH(A, T)                                                  \
+    if (!launched && act == A && tnp == T) {                                        \
+        mlp_narrow_tc_kernel<A, T><<<grid, kNThreads, mlp_narrow_smem(), st>>>(a);  \
+        launched = true;                                                             \
+    }
+    ROSENNA_NARROW_VARIANTS(ROSENNA_NARROW_LAUNCH)
+#undef ROSENNA_NARROW_LAUNCH
+    if (!launched) return cudaErrorInvalidConfiguration;
+    return cudaGetLastError();
+}
+
+}  // namespace rosenna

@@ -37,6 +37,9 @@ struct TcArgs {
     // every layer's Np <= 128: run mlp_tc_dual_kernel (each column group its
     // own tile) instead of splitting one tile's columns between the groups
     int dual;
+    // every layer at most 64 wide with at most 64 inputs and the weights fit in
+    // shared memory: run mlp_narrow_tc_kernel (resident weights, A in TMEM)
+    int narrow;
 };
 
 // One LSTM layer (fLibrary/layers.f90 lstm / lstm_cell) on the tensor cores,
@@ -98,6 +101,11 @@ size_t mlp_tc_smem_bytes();
 bool tc_register_split_ok();
 cudaError_t mlp_tc_configure();
 cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st);
+// Narrow chains (mlp_narrow_tc.cu): whether `a` fits the kernel, its
+// shared-memory attribute, and its launch (one CTA per SM, two tiles at a time).
+bool mlp_narrow_fits(const TcArgs &a);
+cudaError_t mlp_narrow_configure();
+cudaError_t launch_mlp_narrow(const TcArgs &a, int num_sms, cudaStream_t st);
 cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
 
 // Encodes the TMA map of one layer block at `block` (device pointer), with

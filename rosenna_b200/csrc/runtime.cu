@@ -222,7 +222,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                         a.out = ptr[(size_t)s.out] + (int64_t)t * ld[(size_t)s.out];
                         a.ld_out = (int64_t)s.rsub * ld[(size_t)s.out];
                         a.n = cnt;
-                        e = launch_mlp_tc(a, d.num_sms, stream);
+                        e = a.narrow ? launch_mlp_narrow(a, d.num_sms, stream) : launch_mlp_tc(a, d.num_sms, stream);
                         launches++;
                     }
                     if (e == cudaSuccess)
@@ -663,6 +663,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, id);
         CUDA_TRY(configure_kernels());
         CUDA_TRY(mlp_tc_configure());
+        CUDA_TRY(mlp_narrow_configure());
         CUDA_TRY(conv_tc_configure());
         CUDA_TRY(lstm2_tc_configure());
         CUDA_TRY(lstm_dual_tc_configure());
@@ -749,6 +750,10 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             for (int l = 0; l < a.nlayers; l++) narrow = narrow && a.L[l].Np <= 128;
             const char *dual_env = getenv("ROSENNA_TC_DUAL");
             a.dual = narrow && !(dual_env && std::string(dual_env) == "0") ? 1 : 0;
+            // no layer wider than 64 and the weights fit in shared memory: the
+            // resident-weight kernel (ROSENNA_TC_NARROW=0 keeps the others)
+            const char *narrow_env = getenv("ROSENNA_TC_NARROW");
+            a.narrow = mlp_narrow_fits(a) && !(narrow_env && std::string(narrow_env) == "0") ? 1 : 0;
         }
         for (auto &s : d->slots) {
             CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
@@ -1057,7 +1062,9 @@ int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sam
     switch (s.kind) {
         case Step::MLP: {
             const bool dual = s.tc && !g_ctx.devs.empty() && g_ctx.devs[0]->tc_args[(size_t)i].dual;
-            name = s.tc ? (dual ? "mlp_tc_dual_kernel" : "mlp_tc_kernel") : "mlp_ffma_kernel";
+            const bool narrow = s.tc && !g_ctx.devs.empty() && g_ctx.devs[0]->tc_args[(size_t)i].narrow;
+            name = s.tc ? (narrow ? "mlp_narrow_tc_kernel" : dual ? "mlp_tc_dual_kernel" : "mlp_tc_kernel")
+                        : "mlp_ffma_kernel";
             for (auto &l : s.layers) f += 2.0 * l.K * l.M;
             f *= s.rsub;
             break;

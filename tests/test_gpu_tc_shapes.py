@@ -67,6 +67,7 @@ def test_tc_chain_shapes(case, tail, dual, tmp_path, monkeypatch):
     monkeypatch.setenv("ROSENNA_MLP_PATH", "tc")
     monkeypatch.setenv("ROSENNA_TC_TAIL", tail)
     monkeypatch.setenv("ROSENNA_TC_DUAL", dual)
+    monkeypatch.setenv("ROSENNA_TC_NARROW", "0")  # the resident-weight kernel: test_gpu_narrow.py
     d = str(tmp_path)
     widths = build(case, d)
     api.initialize(d)
