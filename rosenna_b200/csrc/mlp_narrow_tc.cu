@@ -15,7 +15,8 @@
 // every MMA, layer by layer, tile 0's then tile 1's, so one tile's epilogue
 // (bias, activation, split) runs while the other tile's MMAs do.  A narrow last
 // layer (N <= 16) runs on the CUDA cores straight from the registers of the
-// layer before.  With each layer's K-step loop unrolled (immediate descriptor
+// layer before.  The next tile's inputs (up to 16) are loaded into registers
+// while the current tile runs.  With each layer's K-step loop unrolled (immediate descriptor
 // offsets), the MMAs issue back to back.
 //
 // TMEM per tile (256 columns at 256g): A hi at +0, A lo at +64, the layer's
@@ -192,6 +193,16 @@ __device__ __forceinline__ void n_layer_out(const TcArgs &p, uint32_t lane_d, co
             if (16 * q + e < nout) p.out[row + (long long)(16 * q + e) * p.ld_out] = tc_act<ACT>(__uint_as_float(v[q][e]) + bias[16 * q + e]);
 }
 
+// The inputs f = 16q..16q+15 of `row` (zero beyond k0 and past the batch).
+__device__ __forceinline__ void n_load_x(const TcArgs &p, int q, int k0, long long row, float (&x)[16]) {
+    const bool valid = row < p.n;
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+        const int f = 16 * q + e;
+        x[e] = (valid && f < k0) ? __ldg(p.in + (long long)f * p.ld_in + row) : 0.f;
+    }
+}
+
 // HACT: the activation of every tensor-core layer; TNP: the CUDA-core last
 // layer's padded width (8 or 16), 0 when the last layer is on the tensor cores.
 template <int HACT, int TNP>
@@ -284,29 +295,35 @@ __global__ void __launch_bounds__(kNThreads, 1) mlp_narrow_tc_kernel(const __gri
         const int g = warp >> 2, r = 32 * (warp & 3) + lane;
         const uint32_t lane_a = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 256u * g, lane_d = lane_a + 128u;
         const int k0 = p.L[0].K;
+        const bool pre = k0 <= 16;  // the next tile's inputs held in registers while this tile runs
+        float xr[16];
+        {
+            const long long t = blockIdx.x + (long long)g * gridDim.x;
+            if (pre && t < ntiles) n_load_x(p, 0, k0, t * 128 + r, xr);
+        }
         uint32_t dcnt = 0;
         bool ok = true;
         for (long long k = 0; ok; k++) {
             const long long t = blockIdx.x + (2 * k + g) * gridDim.x;
             if (t >= ntiles) break;
             const long long row = t * 128 + r;
-            {  // layer 0's A: the inputs, zero beyond K (and past the batch)
-                const bool valid = row < p.n;
+            // layer 0's A: the inputs, zero beyond K (and past the batch)
+            if (pre) {
+                n_put_a16(lane_a, 0, xr);
+                const long long tn = t + 2 * gridDim.x;
+                if (tn < ntiles) n_load_x(p, 0, k0, tn * 128 + r, xr);
+            } else {
 #pragma unroll
                 for (int q = 0; q < kNMaxK / 16; q++)
                     if (16 * q < k0) {
-                        float y[16];
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            const int f = 16 * q + e;
-                            y[e] = (valid && f < k0) ? __ldg(p.in + (long long)f * p.ld_in + row) : 0.f;
-                        }
-                        n_put_a16(lane_a, 16 * q, y);
+                        float x[16];
+                        n_load_x(p, q, k0, row, x);
+                        n_put_a16(lane_a, 16 * q, x);
                     }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                mbar_arrive(bars + kNAFull + g);
             }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(bars + kNAFull + g);
             for (int l = 0; l < nl; l++) {
                 ok = __all_sync(0xffffffffu, mbar_wait(bars + kNDFull + g, dcnt & 1, p.err, 83, (int)k, l));
                 dcnt++;
