@@ -66,14 +66,76 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
         : "memory");
 }
 
+// Packed fp32 pairs (sm_100 f32x2, round to nearest: the same results as the
+// scalar instructions in half the issue slots; the epilogue shares its
+// schedulers with the thread that issues the MMAs).
+__device__ __forceinline__ void n_add2(float &a, float &b, float c, float d) {
+    asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\tadd.rn.f32x2 x, x, y;\n\t"
+        "mov.b64 {%0, %1}, x;\n\t}"
+        : "+f"(a), "+f"(b)
+        : "f"(c), "f"(d));
+}
+__device__ __forceinline__ void n_mul2(float &a, float &b, float c, float d) {
+    asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\tmul.rn.f32x2 x, x, y;\n\t"
+        "mov.b64 {%0, %1}, x;\n\t}"
+        : "+f"(a), "+f"(b)
+        : "f"(c), "f"(d));
+}
+// (a, b) = (a, b) * (c, c) + (d, d)
+__device__ __forceinline__ void n_fma2(float &a, float &b, float c, float d) {
+    asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %2};\n\tmov.b64 z, {%3, %3};\n\t"
+        "fma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
+        : "+f"(a), "+f"(b)
+        : "f"(c), "f"(d));
+}
+// (ra, rb) = (a, b) - (c, d)
+__device__ __forceinline__ void n_sub2(float a, float b, float c, float d, float &ra, float &rb) {
+    asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tsub.rn.f32x2 x, x, y;\n\t"
+        "mov.b64 {%0, %1}, x;\n\t}"
+        : "=f"(ra), "=f"(rb)
+        : "f"(a), "f"(b), "f"(c), "f"(d));
+}
+__device__ __forceinline__ float n_ex2(float x) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x));
+    return e;
+}
+__device__ __forceinline__ float n_rcp(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// The activation of a pair, with the same operations as tc_act (tanh(x) =
+// 1 - 2/(1 + 2^(2 log2(e) x)), sigmoid(x) = 1/(1 + 2^(-log2(e) x))).
+template <int ACT>
+__device__ __forceinline__ void n_act2(float &a, float &b) {
+    if (ACT == 1) {
+        a = a < 0.f ? 0.f : a;
+        b = b < 0.f ? 0.f : b;
+    } else if (ACT == 2 || ACT == 3) {
+        const float k = ACT == 2 ? 2.8853900817779268f : -1.4426950408889634f;
+        n_mul2(a, b, k, k);
+        a = n_ex2(a);
+        b = n_ex2(b);
+        n_add2(a, b, 1.f, 1.f);
+        a = n_rcp(a);
+        b = n_rcp(b);
+        if (ACT == 2) n_fma2(a, b, -2.f, 1.f);
+    }
+}
+
 // Splits 16 values into tf32 hi/lo and stores them at A columns c0.. (hi) and
 // 64 + c0.. (lo) of this thread's lane.
 __device__ __forceinline__ void n_put_a16(uint32_t lane_a, int c0, const float (&v)[16]) {
     uint32_t h[16], l[16];
 #pragma unroll
-    for (int e = 0; e < 16; e++) {
+    for (int e = 0; e < 16; e += 2) {
         h[e] = tf32_rna(v[e]);
-        l[e] = tf32_rna(v[e] - __uint_as_float(h[e]));
+        h[e + 1] = tf32_rna(v[e + 1]);
+        float r0, r1;
+        n_sub2(v[e], v[e + 1], __uint_as_float(h[e]), __uint_as_float(h[e + 1]), r0, r1);
+        l[e] = tf32_rna(r0);
+        l[e + 1] = tf32_rna(r1);
     }
     tmem_st16u(lane_a + (uint32_t)c0, h);
     tmem_st16u(lane_a + 64u + (uint32_t)c0, l);
@@ -121,7 +183,12 @@ __device__ __forceinline__ void n_layer_to_a(uint32_t lane_d, uint32_t lane_a, c
             if (c0 >= np) break;
             float y[16];
 #pragma unroll
-            for (int e = 0; e < 16; e++) y[e] = tc_act<ACT>(__uint_as_float(v[q][e]) + bias[c0 + e]);
+            for (int e = 0; e < 16; e += 2) {
+                y[e] = __uint_as_float(v[q][e]);
+                y[e + 1] = __uint_as_float(v[q][e + 1]);
+                n_add2(y[e], y[e + 1], bias[c0 + e], bias[c0 + e + 1]);
+                n_act2<ACT>(y[e], y[e + 1]);
+            }
             n_put_a16(lane_a, c0, y);
         }
     }
@@ -142,17 +209,23 @@ __device__ __forceinline__ void n_layer_tail(uint32_t lane_d, const float *bias,
         tmem_ld16_nw(lane_d + 16u * q, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
+        for (int e = 0; e < 16; e += 2) {
             const int k = 16 * q + e;
-            const float h = tc_act<ACT>(__uint_as_float(v[e]) + bias[k]);
-            const float4 *w = reinterpret_cast<const float4 *>(tw + k * kTcTailMaxN);
+            float h0 = __uint_as_float(v[e]), h1 = __uint_as_float(v[e + 1]);
+            n_add2(h0, h1, bias[k], bias[k + 1]);
+            n_act2<ACT>(h0, h1);
 #pragma unroll
-            for (int n4 = 0; n4 < TNP / 4; n4++) {
-                const float4 c = w[n4];
-                o[4 * n4] = fmaf(h, c.x, o[4 * n4]);
-                o[4 * n4 + 1] = fmaf(h, c.y, o[4 * n4 + 1]);
-                o[4 * n4 + 2] = fmaf(h, c.z, o[4 * n4 + 2]);
-                o[4 * n4 + 3] = fmaf(h, c.w, o[4 * n4 + 3]);
+            for (int kk = 0; kk < 2; kk++) {
+                const float h = kk ? h1 : h0;
+                const float4 *w = reinterpret_cast<const float4 *>(tw + (k + kk) * kTcTailMaxN);
+#pragma unroll
+                for (int n4 = 0; n4 < TNP / 4; n4++) {
+                    const float4 c = w[n4];
+                    o[4 * n4] = fmaf(h, c.x, o[4 * n4]);
+                    o[4 * n4 + 1] = fmaf(h, c.y, o[4 * n4 + 1]);
+                    o[4 * n4 + 2] = fmaf(h, c.z, o[4 * n4 + 2]);
+                    o[4 * n4 + 3] = fmaf(h, c.w, o[4 * n4 + 3]);
+                }
             }
         }
     }
