@@ -44,10 +44,20 @@ sys.path.insert(0, ROOT)
 # the 126 MB L2; `traffic` = this x the batch.
 NCU_TRAFFIC_PER_SAMPLE = {
     ("wide_mlp", "mlp_tc_kernel"): (69.486592e6 + 10.319616e6) / 1048576,
+    ("small_mlp", "mlp_narrow_tc_kernel"): (42.103296e6 + 0.503040e6) / 1048576,
+    ("lstm", "lstm_dual_tc_kernel"): (105.0368e6 + 5.318144e6) / 65536,
+    ("cnn", "conv_tc_kernel"): (770.143488e6 + 189.512704e6) / 65536,  # conv2, the dominant step
+    ("lstm2", "lstm2_tc_kernel"): (383.717632e6 + 14.7328e6) / 65536,
 }
 NCU_TRAFFIC_NOTE = {
     ("wide_mlp", "mlp_tc_kernel"): "capture at 1,048,576 samples: its 33.5 MB of outputs stayed in L2, so writes are "
                                    "under-counted",
+    ("small_mlp", "mlp_narrow_tc_kernel"): "capture at 1,048,576 samples: its 21 MB of outputs stayed in L2, so "
+                                           "writes are under-counted",
+    ("lstm", "lstm_dual_tc_kernel"): "capture at 65,536 samples (105 MB of inputs), scaled per sample",
+    ("cnn", "conv_tc_kernel"): "conv2 (8->16 channels) at the bench batch; reads are 1.9x its input because "
+                               "neighbouring blocks' patches overlap and part of that reuse misses L2",
+    ("lstm2", "lstm2_tc_kernel"): "capture at 65,536 samples (381 MB of inputs), scaled per sample",
 }
 
 DEFAULT_WORKLOAD = "wide_mlp"
