@@ -88,6 +88,13 @@ __device__ __forceinline__ void n_fma2(float &a, float &b, float c, float d) {
         : "+f"(a), "+f"(b)
         : "f"(c), "f"(d));
 }
+// (a, b) += (h, h) * (c, d)
+__device__ __forceinline__ void n_fma2v(float &a, float &b, float h, float c, float d) {
+    asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %2};\n\tmov.b64 z, {%3, %4};\n\t"
+        "fma.rn.f32x2 x, y, z, x;\n\tmov.b64 {%0, %1}, x;\n\t}"
+        : "+f"(a), "+f"(b)
+        : "f"(h), "f"(c), "f"(d));
+}
 // (ra, rb) = (a, b) - (c, d)
 __device__ __forceinline__ void n_sub2(float a, float b, float c, float d, float &ra, float &rb) {
     asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tsub.rn.f32x2 x, x, y;\n\t"
@@ -221,10 +228,8 @@ __device__ __forceinline__ void n_layer_tail(uint32_t lane_d, const float *bias,
 #pragma unroll
                 for (int n4 = 0; n4 < TNP / 4; n4++) {
                     const float4 c = w[n4];
-                    o[4 * n4] = fmaf(h, c.x, o[4 * n4]);
-                    o[4 * n4 + 1] = fmaf(h, c.y, o[4 * n4 + 1]);
-                    o[4 * n4 + 2] = fmaf(h, c.z, o[4 * n4 + 2]);
-                    o[4 * n4 + 3] = fmaf(h, c.w, o[4 * n4 + 3]);
+                    n_fma2v(o[4 * n4], o[4 * n4 + 1], h, c.x, c.y);
+                    n_fma2v(o[4 * n4 + 2], o[4 * n4 + 3], h, c.z, c.w);
                 }
             }
         }
