@@ -40,6 +40,10 @@ struct TcArgs {
     // every layer at most 64 wide with at most 64 inputs and the weights fit in
     // shared memory: run mlp_narrow_tc_kernel (resident weights, A in TMEM)
     int narrow;
+    // the same with a first layer of more than 64 inputs: mlp_stream_tc_kernel
+    // (that layer's inputs and weights streamed by TMA; xmap set by its launcher)
+    int stream;
+    CUtensorMap xmap;
 };
 
 // One LSTM layer (fLibrary/layers.f90 lstm / lstm_cell) on the tensor cores,
@@ -106,6 +110,12 @@ cudaError_t launch_mlp_tc(const TcArgs &a, int num_sms, cudaStream_t st);
 bool mlp_narrow_fits(const TcArgs &a);
 cudaError_t mlp_narrow_configure();
 cudaError_t launch_mlp_narrow(const TcArgs &a, int num_sms, cudaStream_t st);
+// Narrow chains with a long first layer (mlp_narrow_tc.cu, mlp_stream_tc_kernel).
+// The launch returns cudaErrorNotSupported, launching nothing, when the input
+// array cannot be described by a tensor map (16-byte aligned base and pitch).
+bool mlp_stream_fits(const TcArgs &a);
+cudaError_t mlp_stream_configure();
+cudaError_t launch_mlp_stream(const TcArgs &a, int num_sms, cudaStream_t st);
 cudaError_t launch_lstm_tc(const TcLstmArgs &a, int num_sms, cudaStream_t st);
 
 // Encodes the TMA map of one layer block at `block` (device pointer), with

@@ -222,7 +222,14 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                         a.out = ptr[(size_t)s.out] + (int64_t)t * ld[(size_t)s.out];
                         a.ld_out = (int64_t)s.rsub * ld[(size_t)s.out];
                         a.n = cnt;
-                        e = a.narrow ? launch_mlp_narrow(a, d.num_sms, stream) : launch_mlp_tc(a, d.num_sms, stream);
+                        if (a.narrow) {
+                            e = launch_mlp_narrow(a, d.num_sms, stream);
+                        } else if (a.stream) {
+                            e = launch_mlp_stream(a, d.num_sms, stream);
+                            if (e == cudaErrorNotSupported) e = launch_mlp_tc(a, d.num_sms, stream);  // unaligned input
+                        } else {
+                            e = launch_mlp_tc(a, d.num_sms, stream);
+                        }
                         launches++;
                     }
                     if (e == cudaSuccess)
@@ -664,6 +671,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         CUDA_TRY(configure_kernels());
         CUDA_TRY(mlp_tc_configure());
         CUDA_TRY(mlp_narrow_configure());
+        CUDA_TRY(mlp_stream_configure());
         CUDA_TRY(conv_tc_configure());
         CUDA_TRY(lstm2_tc_configure());
         CUDA_TRY(lstm_dual_tc_configure());
@@ -754,6 +762,9 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             // resident-weight kernel (ROSENNA_TC_NARROW=0 keeps the others)
             const char *narrow_env = getenv("ROSENNA_TC_NARROW");
             a.narrow = mlp_narrow_fits(a) && !(narrow_env && std::string(narrow_env) == "0") ? 1 : 0;
+            // the same with a long first layer streamed by TMA (ROSENNA_TC_STREAM=0 keeps the others)
+            const char *stream_env = getenv("ROSENNA_TC_STREAM");
+            a.stream = !a.narrow && mlp_stream_fits(a) && !(stream_env && std::string(stream_env) == "0") ? 1 : 0;
         }
         for (auto &s : d->slots) {
             CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
@@ -1063,7 +1074,11 @@ int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sam
         case Step::MLP: {
             const bool dual = s.tc && !g_ctx.devs.empty() && g_ctx.devs[0]->tc_args[(size_t)i].dual;
             const bool narrow = s.tc && !g_ctx.devs.empty() && g_ctx.devs[0]->tc_args[(size_t)i].narrow;
-            name = s.tc ? (narrow ? "mlp_narrow_tc_kernel" : dual ? "mlp_tc_dual_kernel" : "mlp_tc_kernel")
+            const bool stream = s.tc && !g_ctx.devs.empty() && g_ctx.devs[0]->tc_args[(size_t)i].stream;
+            name = s.tc ? (narrow   ? "mlp_narrow_tc_kernel"
+                           : stream ? "mlp_stream_tc_kernel"
+                           : dual   ? "mlp_tc_dual_kernel"
+                                    : "mlp_tc_kernel")
                         : "mlp_ffma_kernel";
             for (auto &l : s.layers) f += 2.0 * l.K * l.M;
             f *= s.rsub;
