@@ -276,7 +276,8 @@ def measure(name, n, args, rank, local, world, want_cpu, fp32_ref):
         e1.record(stream)
         torch.cuda.synchronize()
     step_times = api.step_timing_end()
-    t_dev = ranks.max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    t_ranks = ranks.values_over_ranks(e0.elapsed_time(e1) / 1e3)
+    t_dev = max(t_ranks)
     barrier()
     torch.cuda.synchronize()
     value = world * n * args.steps / t_dev
@@ -343,7 +344,9 @@ def measure(name, n, args, rank, local, world, want_cpu, fp32_ref):
     del d_tmp
 
     res = {"workload": f"{w.name}: {w.description}", "batch_per_gpu": n, "value": value, "unit": "samples/s",
-           "ms_per_step": 1e3 * t_dev / args.steps, "e2e": e2e, "roofline": roof, "steps": steps_desc,
+           "ms_per_step": 1e3 * t_dev / args.steps,
+           "ms_per_step_by_rank": [round(1e3 * t / args.steps, 4) for t in t_ranks] if world > 1 else None,
+           "e2e": e2e, "roofline": roof, "steps": steps_desc,
            "gpu_launches": launches, "clocks": clocks, "plan": api.plan_description().strip().splitlines(),
            "l2": f"inputs {sum(x.numel() * 4 for x in ins) / 1e6:.0f} MB + outputs "
                  f"{sum(o.numel() * 4 for o in outs) / 1e6:.0f} MB per step"}
@@ -453,10 +456,11 @@ def main():
                 "cpu_baseline": head["cpu_baseline"], "parity": head["parity"], "clocks": head["clocks"],
                 "steps_detail": head["steps"],
                 "workloads": {head["workload"].split(":")[0]: {k: head[k] for k in (
-                    "workload", "batch_per_gpu", "value", "ms_per_step", "e2e", "roofline", "parity", "cpu_baseline",
-                    "clocks", "gpu_launches")}}}
+                    "workload", "batch_per_gpu", "value", "ms_per_step", "ms_per_step_by_rank", "e2e", "roofline",
+                    "parity", "cpu_baseline", "clocks", "gpu_launches")}}}
         for name, r in rest.items():
-            line["workloads"][name] = {k: r[k] for k in ("workload", "batch_per_gpu", "value", "ms_per_step", "e2e",
+            line["workloads"][name] = {k: r[k] for k in ("workload", "batch_per_gpu", "value", "ms_per_step",
+                                                          "ms_per_step_by_rank", "e2e",
                                                           "roofline", "parity", "cpu_baseline", "clocks",
                                                           "gpu_launches", "steps", "l2")}
         print(json.dumps(line), flush=True)

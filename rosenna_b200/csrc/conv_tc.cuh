@@ -38,6 +38,7 @@ struct ConvTcArgs {
     int *err;                 // [64] status word shared with the other tensor-core kernels
     int C, Hin, Win, pad, OC, Ho, Wo, Hq, Wq, pool, relu;  // pool: 1 max, 2 avg (k = s = 2)
     int ocp, bh, cb, ph, cw, rows, slots;                  // conv_tc_geometry(C, OC)
+    int group;  // sample tiles that take each block in turn (1..64): the unit order
 };
 
 // Whether a conv(+ReLU)+pool step has the shapes conv_tc_kernel covers.
@@ -57,5 +58,36 @@ bool conv_tc_encode_input(ConvTcArgs &a, const float *in, long long ld_in, const
 bool conv_tc_encode_output(ConvTcArgs &a, const char **why);
 cudaError_t conv_tc_configure();
 cudaError_t launch_conv_tc(const ConvTcArgs &a, int num_sms, cudaStream_t st);
+
+// conv_pair_tc_kernel: a conv(+ReLU)+pool step and the conv(+ReLU)+pool step
+// that is the only reader of its output, in one kernel; the first conv's
+// pooled output passes through `mid`, two 128-sample columns per CTA (element
+// (c, y, x) of column s at mid[(c + C2*(y + Hin2*x))*mid_cols + s]).
+struct ConvPairArgs {
+    CUtensorMap map1;   // first conv's input, box {128, cb1, ph1, cw1}
+    CUtensorMap omap1;  // mid as the first conv's pooled output, box {128, ocp1, bh1 / 2, 2}
+    CUtensorMap map2;   // mid as the second conv's input, box {128, cb2, ph2, cw2}
+    CUtensorMap omap2;  // the second conv's pooled output, box {128, ocp2, bh2 / 2, 2}
+    const float *arena;
+    long long s1_off, b1_off, s2_off, b2_off;  // arena offsets: packed first image, bias, second image, bias
+    long long n;
+    int *err;
+    int OC1, Wo1, pad1, relu1, bh1;
+    int OC2, Hin2, Wo2, pad2, relu2, bh2, ph2, nb2;
+    int slots;
+};
+// Whether the two steps' shapes have a conv_pair_tc_kernel instantiation
+// (first: 1 input channel, <= 8 outputs; second: 5..8 inputs, 9..16 outputs).
+bool conv_pair_shape_ok(int C1, int OC1, int pool1, int C2, int OC2, int pool2);
+// Packs a first conv's 3x3 weights with each row's tf32 lo part beside its hi
+// part (kConvTcBFloats / 2 floats); C <= 2.
+void conv_pair_pack1(const float *w, int OC, int C, float *img);
+// Samples per mid column group: mid holds 256 columns per CTA.
+constexpr int kConvPairMidPerCta = 256;
+cudaError_t conv_pair_configure();
+// a1/a2: the two steps as launch_conv_tc would take them (maps encoded, a1's
+// out unused); mid/mid_cols: the per-CTA buffer (grid = mid_cols / 256 at most).
+cudaError_t launch_conv_pair(const ConvTcArgs &a1, long long s1_off, const ConvTcArgs &a2, float *mid,
+                             long long mid_cols, int num_sms, cudaStream_t st, const char **why);
 
 }  // namespace rosenna

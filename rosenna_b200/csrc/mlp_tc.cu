@@ -227,10 +227,8 @@ __device__ __forceinline__ void tail_dots(float (&o)[NP], const float (&acc)[128
                 const float x = tc_act<ACT>(acc[16 * q + e0 + e]);
 #pragma unroll
                 for (int n4 = 0; n4 < NP / 4; n4++) {
-                    o[4 * n4 + 0] = fmaf(x, w4[e][n4].x, o[4 * n4 + 0]);
-                    o[4 * n4 + 1] = fmaf(x, w4[e][n4].y, o[4 * n4 + 1]);
-                    o[4 * n4 + 2] = fmaf(x, w4[e][n4].z, o[4 * n4 + 2]);
-                    o[4 * n4 + 3] = fmaf(x, w4[e][n4].w, o[4 * n4 + 3]);
+                    fma2x(o[4 * n4 + 0], o[4 * n4 + 1], x, w4[e][n4].x, w4[e][n4].y);
+                    fma2x(o[4 * n4 + 2], o[4 * n4 + 3], x, w4[e][n4].z, w4[e][n4].w);
                 }
             }
         }

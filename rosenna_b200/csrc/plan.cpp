@@ -619,6 +619,11 @@ Status Builder::op_conv(const PyVal &e) {  // modelCreator.fpp:103-105, layers.f
         std::vector<float> img((size_t)kConvTcBFloats);
         conv_tc_pack(w.data(), s.OC, s.C, img.data());
         s.ctc_off = put(img.data(), img.size());
+        if (s.C == 1 && s.OC <= 8) {
+            std::vector<float> packed((size_t)kConvTcBFloats / 2);
+            conv_pair_pack1(w.data(), s.OC, s.C, packed.data());
+            s.ctc_packed_off = put(packed.data(), packed.size());
+        }
     }
     s.in = x.buf;
     s.out = new_buf((int64_t)s.OC * s.Ho * s.Wo);
@@ -1113,7 +1118,8 @@ std::string Plan::describe() const {
     for (size_t si = 0; si < steps.size(); si++) {
         const Step &s = steps[si];
         if (s.kind == Step::LSTM && s.fuse_next) o << "lstm2_tc (fused with the next step) ";
-        if (si > 0 && steps[si - 1].fuse_next) o << "(in lstm2_tc) ";
+        if (s.kind == Step::CONV && s.fuse_next) o << "conv_pair_tc (fused with the next step) ";
+        if (si > 0 && steps[si - 1].fuse_next) o << (steps[si - 1].kind == Step::CONV ? "(in conv_pair_tc) " : "(in lstm2_tc) ");
         switch (s.kind) {
             case Step::MLP:
                 o << (s.tc ? "mlp_tc b" : "mlp b") << s.in << "->b" << s.out << " [";

@@ -49,7 +49,9 @@ struct Step {
     int64_t lstm_tc_w_off = -1, lstm_tc_b_off = -1;
     int lstm_tc_Np = 0, lstm_tc_Kp = 0, lstm_tc_nx = 0, lstm_tc_nh = 0;
     // this LSTM step and the next one (which reads only its y) run as one fused
-    // two-layer kernel; its y is never materialised (decided at initialize)
+    // two-layer kernel, its y never materialised; or this CONV step and the
+    // next one (the only reader of its output) run as conv_pair_tc_kernel
+    // (decided at initialize)
     bool fuse_next = false;
     // run on the dual-tile tensor-core kernel (I <= 32, H <= 32; decided at initialize)
     bool lstm_dual = false;
@@ -62,6 +64,9 @@ struct Step {
     // tensor-core (implicit GEMM) B image of a 3x3 stride-1 conv with C <= 8
     // and OC <= 16 (conv_tc.cuh); -1 when not packed
     int64_t ctc_off = -1;
+    // the same weights with each row's tf32 lo part beside its hi part, for the
+    // first conv of a fused pair (one input channel, OC <= 8); -1 when not packed
+    int64_t ctc_packed_off = -1;
 
     // packed weights (MLP: per layer; LSTM/CONV: here)
     int64_t w_off = -1, b_off = -1;

@@ -41,6 +41,8 @@ struct Slot {
     std::vector<float *> scratch;   // per plan buffer (intermediates only)
     std::vector<float *> io;        // per plan buffer: device copies of inputs/outputs (host path)
     int64_t io_cap = 0;
+    float *mid = nullptr;           // conv_pair_tc_kernel's per-CTA buffer (fused conv pairs only)
+    int64_t mid_cols = 0;
 };
 
 struct Device {
@@ -48,7 +50,7 @@ struct Device {
     int num_sms = 148;
     float *arena = nullptr;
     int *err = nullptr;       // tensor-core kernel status word (0 = ok)
-    int *err_host = nullptr;  // pinned copy, refreshed after each tensor-core launch
+    int *err_host = nullptr;  // pinned copy, refreshed at the end of each call that ran a tensor-core kernel
     std::vector<TcArgs> tc_args;  // per plan step (tensor-core MLP steps only)
     std::vector<TcLstmArgs> lstm_args;  // per plan step (tensor-core LSTM steps only)
     std::vector<TcLstm2Args> lstm2_args;  // per plan step (first step of a fused LSTM pair only)
@@ -75,6 +77,9 @@ struct Context {
     std::vector<int64_t> mlp_table_off;        // per step: index into mlp_tables, device offset in arena
     std::vector<int64_t> mlp_table_arena_off;
     std::vector<bool> is_io_in, is_io_out;
+    int conv_group = 4;  // tensor-core conv unit order: sample tiles per block group (ROSENNA_CONV_GROUP)
+    int64_t mid_rows = 0;  // rows of the largest fused conv pair's intermediate (0: no fused pair)
+    int64_t scratch_budget = 0;  // measure_scratch_budget() at initialize
 };
 
 Context g_ctx;
@@ -101,17 +106,26 @@ int ok() {
             return Status::Err(ROSENNA_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));          \
     } while (0)
 
-int64_t scratch_budget_bytes() {
+// Bytes of intermediates a call may allocate: a quarter of the device memory
+// free at initialize, at most 16 GB.  Measured once (cudaMemGetInfo is a call
+// into the kernel driver, which can wait behind other processes' driver work
+// on a shared machine: made on every call it left the GPU idle for
+// milliseconds at a time).
+int64_t measure_scratch_budget() {
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return (int64_t)4 << 30;
     return (int64_t)std::min<size_t>(free_b / 4, (size_t)16 << 30);
 }
+int64_t scratch_budget_bytes() { return g_ctx.scratch_budget > 0 ? g_ctx.scratch_budget : (int64_t)4 << 30; }
 
 void release_device(Device &d) {
     cudaSetDevice(d.id);
     for (auto &s : d.slots) {
         for (auto p : s.scratch) cudaFree(p);
         for (auto p : s.io) cudaFree(p);
+        if (s.mid) cudaFree(s.mid);
+        s.mid = nullptr;
+        s.mid_cols = 0;
         s.scratch.clear();
         s.io.clear();
         s.cap = s.io_cap = 0;
@@ -152,8 +166,10 @@ std::vector<bool> used_buffers() {
     std::vector<bool> used(P.buf_rows.size(), false);
     for (size_t si = 0; si < P.steps.size(); si++) {
         const Step &st = P.steps[si];
+        // (a fused conv pair keeps its intermediate: the two-kernel path takes
+        // calls the pair kernel cannot)
         const bool skip_y = st.kind == Step::LSTM && st.fuse_next;
-        const bool skip_in = si > 0 && P.steps[si - 1].fuse_next;
+        const bool skip_in = si > 0 && P.steps[si - 1].kind == Step::LSTM && P.steps[si - 1].fuse_next;
         for (int b : {st.in, st.out, st.h0, st.c0, st.y, st.hn, st.cn}) {
             if (b < 0 || (skip_y && b == st.y) || (skip_in && b == st.in)) continue;
             used[(size_t)b] = true;
@@ -173,6 +189,19 @@ Status ensure_scratch(Slot &s, int64_t cap) {
         CUDA_TRY(cudaMalloc(&s.scratch[b], sizeof(float) * (size_t)g_ctx.plan.buf_rows[b] * (size_t)cap));
     }
     s.cap = cap;
+    return Status::Ok();
+}
+
+// conv_pair_tc_kernel's buffer: 256 sample columns per SM of the largest
+// fused pair's intermediate rows.
+Status ensure_mid(Slot &s, int num_sms) {
+    const int64_t cols = (int64_t)num_sms * kConvPairMidPerCta;
+    if (g_ctx.mid_rows <= 0 || s.mid_cols >= cols) return Status::Ok();
+    if (s.mid) cudaFree(s.mid);
+    s.mid = nullptr;
+    s.mid_cols = 0;
+    CUDA_TRY(cudaMalloc(&s.mid, sizeof(float) * (size_t)g_ctx.mid_rows * (size_t)cols));
+    s.mid_cols = cols;
     return Status::Ok();
 }
 
@@ -201,14 +230,18 @@ int64_t max_chunk(int64_t n) {
 
 // Runs the plan on `cnt` samples.  ptr[b]/ld[b] address buffer b (row r of
 // sample s at ptr[b][r*ld[b] + s]).
+// `mid`: the slot's conv_pair_tc_kernel buffer, or null (fused conv pairs then
+// run as two kernels).
 Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<int64_t> &ld, int64_t cnt,
-                cudaStream_t stream) {
+                cudaStream_t stream, const Slot *mid) {
     const Plan &P = g_ctx.plan;
     const float *arena = d.arena;
     int64_t launches = 0;
+    bool tc_ran = false;  // a tensor-core kernel ran: refresh the pinned status copy once, after the last step
     for (size_t si = 0; si < P.steps.size(); si++) {
         const Step &s = P.steps[si];
         cudaError_t e = cudaSuccess;
+        bool pair_ran = false;  // this step and the next ran as one kernel
         const bool timed = d.tev_used < (int64_t)d.tev_step.size();
         if (timed && cudaEventRecord(d.tev[(size_t)(2 * d.tev_used)], stream) != cudaSuccess)
             return Status::Err(ROSENNA_ERR_CUDA, "cudaEventRecord (step timing) failed");
@@ -232,8 +265,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                         }
                         launches++;
                     }
-                    if (e == cudaSuccess)
-                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    tc_ran = true;
                     break;
                 }
                 MlpArgs a{};
@@ -276,8 +308,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                     a.n = cnt;
                     e = launch_lstm2_tc(a, d.num_sms, stream);
                     launches++;
-                    if (e == cudaSuccess)
-                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    tc_ran = true;
                     break;
                 }
                 if (s.tc) {
@@ -295,8 +326,7 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                     a.n = cnt;
                     e = s.lstm_dual ? launch_lstm_dual_tc(a, d.num_sms, stream) : launch_lstm_tc(a, d.num_sms, stream);
                     launches++;
-                    if (e == cudaSuccess)
-                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    tc_ran = true;
                     break;
                 }
                 LstmArgs a{};
@@ -326,31 +356,58 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 // the tensor-core conv reads its input and writes its output
                 // through TMA maps: 16-byte aligned bases and sample pitches
                 // (otherwise the CUDA-core kernel below takes the call)
-                if (s.tc && conv_tc_input_ok(ptr[(size_t)s.in], ld[(size_t)s.in]) &&
-                    conv_tc_input_ok(ptr[(size_t)s.out], ld[(size_t)s.out])) {
-                    ConvTcArgs a{};
+                const auto tc_io_ok = [&](const Step &q) {
+                    return conv_tc_input_ok(ptr[(size_t)q.in], ld[(size_t)q.in]) &&
+                           conv_tc_input_ok(ptr[(size_t)q.out], ld[(size_t)q.out]);
+                };
+                const auto tc_args = [&](const Step &q, ConvTcArgs &a) -> Status {
+                    a = ConvTcArgs{};
                     a.arena = arena;
-                    a.bt_off = s.ctc_off;
-                    a.b_off = s.b_off;
-                    a.out = ptr[(size_t)s.out];
-                    a.ld_out = ld[(size_t)s.out];
-                    a.so_c = s.so_c; a.so_h = s.so_h; a.so_w = s.so_w;
+                    a.bt_off = q.ctc_off;
+                    a.b_off = q.b_off;
+                    a.out = ptr[(size_t)q.out];
+                    a.ld_out = ld[(size_t)q.out];
+                    a.so_c = q.so_c; a.so_h = q.so_h; a.so_w = q.so_w;
                     a.n = cnt;
                     a.err = d.err;
-                    a.C = s.C; a.Hin = s.Hin; a.Win = s.Win; a.pad = s.pad_h; a.OC = s.OC;
-                    a.Ho = s.Ho; a.Wo = s.Wo; a.Hq = s.Hq; a.Wq = s.Wq; a.pool = s.pool; a.relu = s.relu ? 1 : 0;
-                    const ConvTcGeom geo = conv_tc_geometry(s.C, s.OC);
+                    a.C = q.C; a.Hin = q.Hin; a.Win = q.Win; a.pad = q.pad_h; a.OC = q.OC;
+                    a.Ho = q.Ho; a.Wo = q.Wo; a.Hq = q.Hq; a.Wq = q.Wq; a.pool = q.pool; a.relu = q.relu ? 1 : 0;
+                    const ConvTcGeom geo = conv_tc_geometry(q.C, q.OC);
                     a.ocp = geo.ocp; a.bh = geo.bh; a.cb = geo.cb; a.ph = geo.ph; a.cw = geo.cw;
                     a.rows = geo.rows; a.slots = geo.slots;
+                    a.group = g_ctx.conv_group;
                     const char *why = nullptr;
-                    if (!conv_tc_encode_input(a, ptr[(size_t)s.in], ld[(size_t)s.in], &why))
+                    if (!conv_tc_encode_input(a, ptr[(size_t)q.in], ld[(size_t)q.in], &why))
                         return Status::Err(ROSENNA_ERR_CUDA, std::string("conv_tc input map: ") + (why ? why : "?"));
                     if (!conv_tc_encode_output(a, &why))
                         return Status::Err(ROSENNA_ERR_CUDA, std::string("conv_tc output map: ") + (why ? why : "?"));
+                    return Status::Ok();
+                };
+                // this conv and the next one as conv_pair_tc_kernel, its
+                // output passing through the slot's small per-CTA buffer
+                if (s.fuse_next && mid && mid->mid && si + 1 < P.steps.size() && s.tc && P.steps[si + 1].tc &&
+                    tc_io_ok(s) && tc_io_ok(P.steps[si + 1])) {
+                    const Step &s2 = P.steps[si + 1];
+                    ConvTcArgs a1, a2;
+                    Status st = tc_args(s, a1);
+                    if (st.ok()) st = tc_args(s2, a2);
+                    if (!st.ok()) return st;
+                    const char *why = nullptr;
+                    e = launch_conv_pair(a1, s.ctc_packed_off, a2, mid->mid, mid->mid_cols, d.num_sms, stream, &why);
+                    if (e != cudaSuccess && why)
+                        return Status::Err(ROSENNA_ERR_CUDA, std::string(why) + ": " + cudaGetErrorString(e));
+                    launches++;
+                    tc_ran = true;
+                    pair_ran = true;
+                    break;
+                }
+                if (s.tc && tc_io_ok(s)) {
+                    ConvTcArgs a;
+                    Status st = tc_args(s, a);
+                    if (!st.ok()) return st;
                     e = launch_conv_tc(a, d.num_sms, stream);
                     launches++;
-                    if (e == cudaSuccess)
-                        e = cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+                    tc_ran = true;
                     break;
                 }
                 ConvArgs a{};
@@ -402,8 +459,10 @@ Status run_plan(Device &d, const std::vector<float *> &ptr, const std::vector<in
                 return Status::Err(ROSENNA_ERR_CUDA, "cudaEventRecord (step timing) failed");
             d.tev_step[(size_t)d.tev_used++] = (int)si;
         }
-        if (s.kind == Step::LSTM && s.fuse_next) si++;  // the next layer ran inside the fused kernel
+        if ((s.kind == Step::LSTM && s.fuse_next) || pair_ran) si++;  // the next step ran inside the fused kernel
     }
+    if (tc_ran && cudaMemcpyAsync(d.err_host, d.err, 64 * sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+        return Status::Err(ROSENNA_ERR_CUDA, "status word copy failed");
     g_launches += launches;
     return Status::Ok();
 }
@@ -474,6 +533,7 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
     for (int k = 0; k < kSlots; k++) {
         Status st = ensure_scratch(d.slots[k], std::min(chunk, total));
         if (!st.ok()) return st;
+        if (!(st = ensure_mid(d.slots[k], d.num_sms)).ok()) return st;
         if (!(st = ensure_io(d.slots[k], std::min(chunk, total))).ok()) return st;
     }
     int64_t ci = 0;
@@ -494,7 +554,7 @@ Status host_range(Device &d, int64_t n, int64_t a, int64_t b, const float *const
                                        sizeof(float) * pre * (size_t)n, sizeof(float) * pre * (size_t)cnt,
                                        (size_t)io.rows / pre, cudaMemcpyHostToDevice, s.stream));
         }
-        Status st = run_plan(d, ptr, ld, cnt, s.stream);
+        Status st = run_plan(d, ptr, ld, cnt, s.stream, &s);
         if (!st.ok()) return st;
         for (size_t i = 0; i < P.outputs.size(); i++) {
             const IoDesc &io = P.outputs[i];
@@ -639,12 +699,46 @@ Status do_initialize(const std::string &model, const std::string &weights, const
     // tensor cores for every shape they cover
     const char *cpath = getenv("ROSENNA_CONV_PATH");
     const std::string conv_path = cpath ? cpath : "";
+    const char *genv = getenv("ROSENNA_CONV_GROUP");
+    g_ctx.conv_group = 4;
+    if (genv && atoi(genv) >= 1 && atoi(genv) <= 64) g_ctx.conv_group = atoi(genv);
     for (auto &s : P.steps)
         if (s.kind == Step::CONV)
             s.tc = tc_ok && s.conv && s.ctc_off >= 0 && conv_path != "tiled" && conv_path != "direct" &&
                    (conv_path == "tc" || s.C == 1 || s.C >= 4) &&
                    conv_tc_shape_ok(s.KS, s.str_h, s.str_w, s.pad_h, s.pad_w, s.C, s.OC, s.pool, s.pk, s.pstr_h,
                                     s.pstr_w, s.ppad_h, s.ppad_w, s.Ho, s.Wo);
+    // ROSENNA_CONV_FUSE=1: a tensor-core conv whose only reader is the next
+    // tensor-core conv runs with it as conv_pair_tc_kernel (shapes it
+    // instantiates).  Off by default: both convs are bound by their chunk
+    // pipeline (split into TMEM, MMA issue), not by the intermediate's DRAM
+    // traffic, and the pair kernel, with fewer chunk slots beside both weight
+    // images, measured slower than the two kernels (0.80 ms against 0.60 ms
+    // for the 28x28 CNN's convs at 65,536 samples)
+    const char *cfenv = getenv("ROSENNA_CONV_FUSE");
+    const bool cfuse_ok = cfenv && std::string(cfenv) == "1";
+    g_ctx.mid_rows = 0;
+    for (size_t si = 0; si + 1 < P.steps.size(); si++) {
+        Step &a = P.steps[si];
+        const Step &b = P.steps[si + 1];
+        if (a.kind != Step::CONV) continue;
+        a.fuse_next = false;
+        if (!cfuse_ok || b.kind != Step::CONV || !a.tc || !b.tc || b.in != a.out || a.ctc_packed_off < 0 ||
+            a.Hq != b.Hin || a.Wq != b.Win || !conv_pair_shape_ok(a.C, a.OC, a.pool, b.C, b.OC, b.pool))
+            continue;
+        bool other_reader = false;
+        for (size_t k = 0; k < P.steps.size(); k++) {
+            const Step &q = P.steps[k];
+            if (k != si + 1 && (q.in == a.out || q.h0 == a.out || q.c0 == a.out)) other_reader = true;
+        }
+        for (auto *v : {&P.inputs, &P.outputs})
+            for (auto &io : *v)
+                if (io.buf == a.out) other_reader = true;
+        if (other_reader) continue;
+        a.fuse_next = true;
+        g_ctx.mid_rows = std::max<int64_t>(g_ctx.mid_rows, (int64_t)b.C * b.Hin * b.Win);
+        si++;  // the second conv is not the first of another pair
+    }
     g_ctx.is_io_in.assign(P.buf_rows.size(), false);
     g_ctx.is_io_out.assign(P.buf_rows.size(), false);
     for (auto &io : P.inputs) g_ctx.is_io_in[(size_t)io.buf] = true;
@@ -673,6 +767,7 @@ Status do_initialize(const std::string &model, const std::string &weights, const
         CUDA_TRY(mlp_narrow_configure());
         CUDA_TRY(mlp_stream_configure());
         CUDA_TRY(conv_tc_configure());
+        CUDA_TRY(conv_pair_configure());
         CUDA_TRY(lstm2_tc_configure());
         CUDA_TRY(lstm_dual_tc_configure());
         CUDA_TRY(cudaMalloc(&d->arena, sizeof(float) * std::max<size_t>(P.arena.size(), 4)));
@@ -771,6 +866,8 @@ Status do_initialize(const std::string &model, const std::string &weights, const
             CUDA_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
         }
         noalloc_setup(*d);
+        // the first device's budget stands for all (the same GPU model)
+        if (g_ctx.devs.empty()) g_ctx.scratch_budget = measure_scratch_budget();
         g_ctx.devs.push_back(std::move(d));
     }
     cudaSetDevice(cur);
@@ -974,6 +1071,7 @@ int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *c
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int64_t chunk = max_chunk(n);
     st = ensure_scratch(d->slots[0], chunk);
+    if (st.ok()) st = ensure_mid(d->slots[0], d->num_sms);
     if (!st.ok()) return report(st);
     // the scratch buffers are shared by every device-path call on this device
     if (cudaStreamWaitEvent(s, d->slots[0].done, 0) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaStreamWaitEvent failed");
@@ -992,7 +1090,7 @@ int rosenna_use_model_device_f32(int64_t n, const float *const *inputs, float *c
             ptr[(size_t)P.outputs[i].buf] = outputs[i] + c0;
             ld[(size_t)P.outputs[i].buf] = n;
         }
-        st = run_plan(*d, ptr, ld, cnt, s);
+        st = run_plan(*d, ptr, ld, cnt, s, &d->slots[0]);
         if (!st.ok()) return report(st);
     }
     if (cudaEventRecord(d->slots[0].done, s) != cudaSuccess) return fail(ROSENNA_ERR_CUDA, "cudaEventRecord failed");
@@ -1102,6 +1200,15 @@ int rosenna_step_info(int i, char *kernel, int kernel_len, double *flops_per_sam
             a.str_h = s.str_h; a.str_w = s.str_w; a.pool = s.pool; a.pk = s.pk;
             name = s.tc ? "conv_tc_kernel" : conv_kernel_name(a);
             if (s.conv) f = 2.0 * s.Ho * s.Wo * s.OC * (double)s.C * s.KS * s.KS;
+            if (s.fuse_next) {  // both convs
+                const Step &s2 = g_ctx.plan.steps[(size_t)i + 1];
+                name = "conv_pair_tc_kernel";
+                f += 2.0 * s2.Ho * s2.Wo * s2.OC * (double)s2.C * s2.KS * s2.KS;
+            } else if (i > 0 && g_ctx.plan.steps[(size_t)i - 1].kind == Step::CONV &&
+                       g_ctx.plan.steps[(size_t)i - 1].fuse_next) {
+                name = "(in conv_pair_tc_kernel)";
+                f = 0;
+            }
             break;
         }
         case Step::GATHER:
@@ -1176,6 +1283,6 @@ extern "C" int rosenna_use_model_device_noalloc_f32(int64_t n, const float *cons
         if (used[b] && is_scratch((int)b)) ptr[b] = reinterpret_cast<float *>(base + off[b]);
     for (size_t i = 0; i < P.inputs.size(); i++) ptr[(size_t)P.inputs[i].buf] = const_cast<float *>(inputs[i]);
     for (size_t i = 0; i < P.outputs.size(); i++) ptr[(size_t)P.outputs[i].buf] = outputs[i];
-    st = run_plan(*d, ptr, ld, n, reinterpret_cast<cudaStream_t>(stream));
+    st = run_plan(*d, ptr, ld, n, reinterpret_cast<cudaStream_t>(stream), nullptr);  // no mid: two conv kernels
     return report(st);
 }

@@ -196,6 +196,15 @@ __device__ __forceinline__ void add2(float &a0, float &a1, uint32_t b0, uint32_t
         : "r"(b0), "r"(b1));
 }
 
+// (a0, a1) += x * (w0, w1) on one packed f32x2 FMA (round to nearest: the
+// results of two scalar FMAs in one issue slot).
+__device__ __forceinline__ void fma2x(float &a0, float &a1, float x, float w0, float w1) {
+    asm("{\n\t.reg .b64 a, b, c;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %2};\n\tmov.b64 c, {%3, %4};\n\t"
+        "fma.rn.f32x2 a, b, c, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(x), "f"(w0), "f"(w1));
+}
+
 // K-major operand, 128-byte swizzle: 8-row atoms of 1024 bytes (SBO), rows of
 // 128 bytes; LBO unused for swizzled K-major (set to 16 bytes); version 1.
 __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {

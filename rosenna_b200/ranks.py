@@ -109,6 +109,19 @@ def max_over_ranks(x: float, group=None) -> float:
     return float(t.item())
 
 
+def values_over_ranks(x: float, group=None) -> List[float]:
+    """Every rank's x, in rank order (a per-rank record beside the max)."""
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return [float(x)]
+    dev = _collective_device(group)
+    parts = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, torch.tensor([float(x)], dtype=torch.float64, device=dev), group=group)
+    return [float(p.item()) for p in parts]
+
+
 def _parse_cpulist(text: str) -> List[int]:
     cpus: List[int] = []
     for part in text.strip().split(","):

@@ -83,6 +83,7 @@ def _gloo_rank(rank, world, port, model_dirs, q):
             full = ranks.gather_shards(local, n)
             q.put((r, name, n, a, b, full))
         q.put((r, "max", ranks.max_over_ranks(0.25 + r)))
+        q.put((r, "all", ranks.values_over_ranks(0.5 * r)))
     finally:
         dist.destroy_process_group()
 
@@ -101,12 +102,13 @@ def test_two_gloo_ranks_shard_gather_and_time(tmp_path):
     procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, model_dirs, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = [q.get(timeout=240) for _ in range(world * (len(CASES) + 1))]
+    got = [q.get(timeout=240) for _ in range(world * (len(CASES) + 2))]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     for rank in range(world):
         assert [g[2] for g in got if g[0] == rank and g[1] == "max"] == [0.25 + world - 1]
+        assert [g[2] for g in got if g[0] == rank and g[1] == "all"] == [[0.5 * r for r in range(world)]]
     for name, n in CASES:
         want = oracle_runner(model_dirs[name])(workloads.make_inputs(name, n), n)
         rows = {g[0]: g for g in got if g[1] == name and g[2] == n}
