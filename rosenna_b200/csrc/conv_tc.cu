@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kCtThreads, 1) conv_tc_kernel(const __grid_con
                     for (int e = 0; e < 8; e++) {
                         const float x = src[(j + e) * 128];
                         h[e] = tf32_rna(x);
-                        l[e] = tf32_rna(x - __uint_as_float(h[e]));
+                        l[e] = tf32_lo(x, h[e]);
                     }
                     tmem_st8(acol + (uint32_t)j, h);
                     tmem_st8(acol + 32u + (uint32_t)j, l);
@@ -546,7 +546,7 @@ __device__ __forceinline__ bool pair_split_unit(uint64_t *bars, const uint8_t *r
             for (int e = 0; e < 8; e++) {
                 const float x = src[(j + e) * 128];
                 h[e] = tf32_rna(x);
-                l[e] = tf32_rna(x - __uint_as_float(h[e]));
+                l[e] = tf32_lo(x, h[e]);
             }
             tmem_st8(acol + (uint32_t)j, h);
             tmem_st8(acol + 32u + (uint32_t)j, l);

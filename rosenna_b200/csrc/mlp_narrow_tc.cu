@@ -141,8 +141,8 @@ __device__ __forceinline__ void n_put_a16(uint32_t lane_a, int c0, const float (
         h[e + 1] = tf32_rna(v[e + 1]);
         float r0, r1;
         n_sub2(v[e], v[e + 1], __uint_as_float(h[e]), __uint_as_float(h[e + 1]), r0, r1);
-        l[e] = tf32_rna(r0);
-        l[e + 1] = tf32_rna(r1);
+        l[e] = __float_as_uint(r0);  // left unrounded, as tf32_lo
+        l[e + 1] = __float_as_uint(r1);
     }
     tmem_st16u(lane_a + (uint32_t)c0, h);
     tmem_st16u(lane_a + 64u + (uint32_t)c0, l);

@@ -3,10 +3,11 @@
 //
 // Math (fLibrary/layers.f90:11-23 linear_layer + activation_funcs.f90, per
 // layer): Y[s][n] = act(sum_k A[s][k] W[n][k] + b[n]).  With A = Ah + Al and
-// W = Wh + Wl, where Xh = tf32_round(X) and Xl = tf32_round(X - Xh), the
-// product is taken as Al*Wh + Ah*Wl + Ah*Wh (the Al*Wl term is below 2^-22
-// relative), accumulated in fp32 in tensor memory: fp32-level accuracy from
-// the TF32 tensor pipe.
+// W = Wh + Wl, where Xh = tf32_round(X) and Xl = tf32_round(X - Xh) (for
+// the activations Xl = X - Xh, whose low bits the tensor core drops itself:
+// tf32_lo), the product is taken as Al*Wh + Ah*Wl + Ah*Wh (the Al*Wl term is
+// below 2^-22 relative), accumulated in fp32 in tensor memory: fp32-level
+// accuracy from the TF32 tensor pipe.
 //
 // Per CTA (one per SM, persistent over tiles of 128 samples): two groups of
 // four warps; group g owns output columns [128g, 128g+128) and thread r of a

@@ -228,6 +228,13 @@ __device__ __forceinline__ uint32_t idesc_tf32(int N) {
 // A carry out of the mantissa rounds up into the exponent, as it should (to
 // infinity past the largest float).
 __device__ __forceinline__ uint32_t tf32_rna(float x) { return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u; }
+// The lo part of an activation's split, x - hi (exact in fp32), left
+// unrounded: the tensor core reads a tf32 operand's top 19 bits, so it drops
+// lo's low 13 bits itself.  |lo| <= 2^-11 |x| once hi is rounded to nearest,
+// so what it drops is below 2^-22 |x|, with the sign of lo (either way, not a
+// bias); rounding lo here as well (2^-23) cost three more instructions per
+// value on the epilogue and split paths.
+__device__ __forceinline__ uint32_t tf32_lo(float x, uint32_t hi) { return __float_as_uint(x - __uint_as_float(hi)); }
 
 __device__ __forceinline__ float tc_tanh(float x) {
     float e, r;
@@ -259,7 +266,7 @@ __device__ __forceinline__ void put_a16(uint8_t *ahi, uint8_t *alo, int r, int k
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             h[e] = tf32_rna(v[4 * q + e]);
-            l[e] = tf32_rna(v[4 * q + e] - __uint_as_float(h[e]));
+            l[e] = tf32_lo(v[4 * q + e], h[e]);
         }
         const uint32_t chunk = (uint32_t)((k0 >> 2) + q);
         const uint32_t off = row + ((chunk ^ (uint32_t)(r & 7)) << 4);
