@@ -87,7 +87,7 @@ def test_pair_shapes(H, pad1, pool1, C2, OC2, pad2, pool2, tmp_path, monkeypatch
 
 def test_pair_device_entry_matches_host(tmp_path, monkeypatch):
     """The device entry point (slot 0's buffer, caller's stream) and the host
-    entry point (chunks over three streams, a buffer per stream) agree."""
+    entry point (chunks over four streams, a buffer per stream) agree."""
     monkeypatch.setenv("ROSENNA_CONV_FUSE", "1")
     workloads.write_model("cnn", str(tmp_path))
     api.initialize(str(tmp_path))

@@ -61,7 +61,7 @@ def test_full_batch_parity(name, tmp_path):
 
 @pytest.mark.parametrize("name", ["small_mlp", "wide_mlp", "lstm", "cnn"])
 def test_full_batch_host_path_matches_device_path(name, tmp_path):
-    """rosenna_use_model_f32 (host arrays, chunked over three streams) at the
+    """rosenna_use_model_f32 (host arrays, chunked over four streams) at the
     full batch gives the device entry point's outputs bit for bit."""
     w = workloads.WORKLOADS[name]
     n = w.batch
