@@ -44,9 +44,9 @@ sys.path.insert(0, ROOT)
 # the 126 MB L2; `traffic` = this x the batch.
 NCU_TRAFFIC_PER_SAMPLE = {
     ("wide_mlp", "mlp_tc_kernel"): (69.464576e6 + 12.883968e6) / 1048576,
-    ("small_mlp", "mlp_narrow_tc_kernel"): (42.103296e6 + 0.503040e6) / 1048576,
+    ("small_mlp", "mlp_narrow_tc_kernel"): (42.096896e6 + 0.306944e6) / 1048576,
     ("lstm", "lstm_dual_tc_kernel"): (105.0368e6 + 5.318144e6) / 65536,
-    ("cnn", "conv_tc_kernel"): (770.143488e6 + 189.512704e6) / 65536,  # conv2, the dominant step
+    ("cnn", "conv_tc_kernel"): (769.880064e6 + 190.848768e6) / 65536,  # conv2, the dominant step
     ("lstm2", "lstm2_tc_kernel"): (383.717632e6 + 14.7328e6) / 65536,
 }
 NCU_TRAFFIC_NOTE = {
